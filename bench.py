@@ -1,0 +1,319 @@
+"""Trie-verify step benchmark.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Workload (config 3): random-init 28-layer Qwen3-style decoder (hidden 3584,
+28 q / 4 kv heads of 128, FFN 18944, vocab 152,064, RoPE theta 1e6, weights
+~ N(0, 0.02), bf16); a 3,000-token prefix of seeded random ids, prefilled by
+the engine; a 128-node trie of 4 chains of 32 with seeded shared prefixes, one
+of them the model's own greedy continuation, so each verify step commits 32
+tokens. A step = one verify forward over the trie + greedy choice (+ in the
+e2e loop: host->device trie arrays, device->host ids, the host acceptance
+walk and the KV compaction). Metric: committed tokens/s (whole job); latency
+in ms_per_step. Weights (14.1 GB per step) exceed L2 (126 MB), so no flush
+is needed between steps.
+
+N > 1: one process per GPU (torchrun), independent replicas (frame streams)
+with no collective on the data path; the timed region is bracketed by a
+barrier and the max over ranks is reported.
+
+--impl reference: the reference's CPU path (the numpy oracle restating it,
+oracle/) on the host cores, on a bounded sample of the same step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+PROMPT = 3000
+NODES = 128
+CHAIN = 32
+KERNELS_PER_LAYER = 9          # qkv gemm, qkv finish, attn prefix, attn nodes, o gemm, resid, gu gemm, down gemm, resid
+KERNELS_FIXED = 3              # embed+norm, lm_head gemm, greedy
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def config_block(n):
+    return {"workload": "config3: trie verify step, 28-layer 7B-class decoder, prefix 3000, 128-node trie",
+            "model": "qwen3-style random-init hidden3584 L28 H28/4 D128 F18944 V152064",
+            "prefix": PROMPT, "trie_nodes": NODES, "committed_per_step": CHAIN, "global_batch": n,
+            "parallelism": f"replicas{n}", "l2": "inputs larger than L2 (14.1 GB weights per step)"}
+
+
+# ------------------------------------------------------------------ CPU sample (oracle)
+def cpu_sample(steps, warmup, seed=0):
+    """One decoder layer of the step (128 rows vs the 3000-token prefix) plus 1/28
+    of the lm_head rows, in the numpy oracle; a step is 28 such samples."""
+    from oracle import model as omodel
+    from oracle.bf16 import round_bf16
+    from oracle.inputs import chain_seqs, top_up
+    from respect_b200.candidates.trie import build_trie
+    rng = np.random.default_rng(seed)
+    h, H, HK, D, F, V = 3584, 28, 4, 128, 18944, 152064
+
+    def nrm(*s):
+        return round_bf16(rng.standard_normal(s, dtype=np.float32) * np.float32(0.02))
+    lw = dict(wq=nrm(H * D, h), wk=nrm(HK * D, h), wv=nrm(HK * D, h), wo=nrm(h, H * D), wg=nrm(F, h), wu=nrm(F, h),
+              wd=nrm(h, F), in_norm=np.ones(h, np.float32), post_norm=np.ones(h, np.float32),
+              q_norm=np.ones(D, np.float32), k_norm=np.ones(D, np.float32))
+    W = dict(embed=nrm(V // 28, h), lm_head=nrm(V // 28, h), final_norm=np.ones(h, np.float32), layers=[lw])
+    cfg = dict(n_heads=H, n_kv_heads=HK, head_dim=D, rms_eps=1e-6, rope_theta=1e6)
+    tree = build_trie(top_up(rng, chain_seqs(rng, 4, CHAIN, V // 28), NODES, V // 28))
+    kc = [round_bf16(rng.standard_normal((HK, PROMPT + NODES, D), dtype=np.float32))]
+    vc = [round_bf16(rng.standard_normal((HK, PROMPT + NODES, D), dtype=np.float32))]
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        omodel.verify_step(W, cfg, tree.tokens(), tree.parents(), tree.depths(), PROMPT, 0, kc, vc)
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    t_step = 28 * statistics.median(times)
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return dict(value=CHAIN / t_step, unit="committed tokens/s", cores=threads, kind="port",
+                sample=("numpy oracle (oracle/model.py), one full-size decoder layer of the config-3 step "
+                        "(128 trie rows vs a 3000-token prefix) plus 1/28 of the lm_head rows; "
+                        f"step time = 28 x median of {steps} samples = {t_step:.2f} s"),
+                ms_per_step=t_step * 1e3)
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    steps = max(1, min(args.steps, 3))
+    warm = max(0, min(args.warmup, 1))
+    cb = cpu_sample(steps, warm)
+    line = {"metric": "committed tokens/s (trie-verify step)", "value": cb["value"], "unit": cb["unit"],
+            "impl": "reference", "n_gpus": args.gpus, "steps": steps, "warmup": warm,
+            "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded)", "config": config_block(args.gpus),
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ clocks
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for ln in self.path.read_text().splitlines():
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) >= 9:
+                rows.append(p)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ native arm
+def run_native(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+
+    from oracle.inputs import top_up
+    from respect_b200 import _lib
+    from respect_b200.candidates.trie import build_trie
+    from respect_b200.decoding.acceptance import walk
+    from respect_b200.decoding.engine import DecoderConfig, DecoderWeights, VerifyEngine
+    from respect_b200.kernels.gemm import linear
+
+    cfg = DecoderConfig.baseline_7b()
+    w = DecoderWeights.random(cfg, dev, seed=0)
+    eng = VerifyEngine(w, max_rows=NODES, max_slots=PROMPT + 1024)
+    rng = np.random.default_rng(100 + rank)
+    eng.prefill(rng.integers(0, cfg.vocab, PROMPT))
+    # the model's own greedy continuation (1-token steps) becomes one chain
+    first = int(rng.integers(0, cfg.vocab))
+    toks = [first]
+    for t in range(CHAIN):
+        eng.step(np.array([toks[-1]], np.int32), np.array([-1], np.int32), np.array([0], np.int32), t, PROMPT)
+        toks.append(int(eng.fetch_ids(1)[0]))
+    seqs = [tuple(toks[:CHAIN])]
+    while len(seqs) < 4:
+        share = int(rng.integers(1, CHAIN))
+        cand = tuple(toks[:share]) + tuple(int(x) for x in rng.integers(0, cfg.vocab, CHAIN - share))
+        if len(build_trie(seqs + [cand]).nodes) <= NODES:
+            seqs.append(cand)
+    tree = build_trie(top_up(rng, seqs, NODES, cfg.vocab))
+    assert len(tree.nodes) == NODES
+    ids_d = torch.from_numpy(tree.tokens().astype(np.int32)).to(dev)
+    par_d = torch.from_numpy(tree.parents()).to(dev)
+    dep_d = torch.from_numpy(tree.depths()).to(dev)
+    st = torch.cuda.current_stream(dev)
+
+    def device_step():
+        eng.step(ids_d, par_d, dep_d, 0, PROMPT)
+
+    # correctness of the timed configuration: the AR chain is accepted in full
+    am = eng.verify(tree, PROMPT, 0)
+    path, acc, rec = walk(tree, first, 1 << 30, -1, lambda a, ch: int(am[ch]))
+    committed = len(acc)
+    assert acc == toks[:CHAIN] and committed == CHAIN, "trie verify disagrees with AR decoding"
+
+    for _ in range(args.warmup):
+        device_step()
+    torch.cuda.synchronize()
+
+    def timed(fn, k):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(k):
+            fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    with Clocks(local) as clk:
+        ms = timed(device_step, args.steps)
+    clocks = clk.summary()
+    ms_step = ms / args.steps
+    value = world * committed * args.steps / (ms / 1e3)
+
+    # e2e: the public verify call with host trie arrays, host read-back, host walk, compaction
+    def e2e_step():
+        am = eng.verify(tree, PROMPT, 0)
+        p, a, r = walk(tree, first, 1 << 30, -1, lambda x, ch: int(am[ch]))
+        eng.compact(p, PROMPT, 0)
+
+    k2 = args.e2e_steps or max(1, args.steps // 3)
+    for _ in range(2):
+        e2e_step()
+    ms2 = timed(e2e_step, k2)
+    e2e = {"value": world * committed * k2 / (ms2 / 1e3), "unit": "committed tokens/s",
+           "ms_per_step": ms2 / k2, "h2d_bytes_per_step": 32 + 3 * 4 * NODES, "d2h_bytes_per_step": 8 * NODES}
+
+    # roofline of the dominant kernel: the gate|up weight-streaming GEMM of a layer
+    hbm, tf, src = measured_peaks()
+    xg = torch.randn(NODES, cfg.hidden, device=dev, generator=torch.Generator(device=dev).manual_seed(5)).to(torch.bfloat16)
+    wgu = w.layers[0]["wgu"]
+    for _ in range(3):
+        linear(xg, wgu)
+    reps = 50
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    bufs = [w.layers[i]["wgu"] for i in range(cfg.n_layers)]
+    e0.record(st)
+    for i in range(reps):
+        linear(xg, bufs[i % len(bufs)])      # rotate layers: every launch streams its weights from HBM
+    e1.record(st)
+    torch.cuda.synchronize()
+    gu_ms = e0.elapsed_time(e1) / reps
+    gu_bytes = wgu.numel() * 2 + xg.numel() * 2 + NODES * wgu.shape[0] * 2
+    achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
+    step_bytes = cfg.weight_bytes_per_step() + 2 * cfg.n_layers * 2 * cfg.n_kv_heads * (PROMPT + NODES) * 128 \
+        + NODES * cfg.vocab * 4
+    roof = {"bound": "hbm", "kernel": "gemm_kernel<256,1,kEpiStoreBF16> gate|up N=37888 K=3584 M=128",
+            "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "peak_source": src,
+            "traffic": None, "algorithmic_bytes": gu_bytes, "launch_ms": gu_ms}
+    step_roof = {"bound": "hbm", "algorithmic_bytes": step_bytes, "achieved": step_bytes / (ms_step * 1e-3) / 1e9,
+                 "peak": hbm, "unit": "GB/s", "frac": step_bytes / (ms_step * 1e-3) / 1e9 / hbm,
+                 "floor_ms": step_bytes / (hbm * 1e9) * 1e3}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_sample(2, 1)
+        cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    err = _lib.device_error()
+    launches = args.steps * (KERNELS_FIXED + KERNELS_PER_LAYER * cfg.n_layers)
+    if rank == 0:
+        line = {"metric": "committed tokens/s (trie-verify step)", "value": value, "unit": "committed tokens/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded ids, random-init weights)", "config": config_block(world),
+                "e2e": e2e, "gpu_launches": launches, "roofline": roof, "step_roofline": step_roof,
+                "cpu_baseline": cpu, "clocks": clocks, "device_error": err}
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_native(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,335 @@
+// Deterministic trie-verification attention (respect/kernels/attention.py:15-96).
+//
+// Phase 1 (prefix, keys [0, NP)): the prefix is cut into chunks of
+// kPrefixChunk keys at ABSOLUTE positions (chunk c = [c*C, (c+1)*C)), each
+// chunk reduced by an online softmax over fixed key tiles into a partial
+// (max, sum, acc[D]) per query row. Chunk boundaries depend on NP only.
+// Phase 2 (per query row, one warp): merge the chunk partials in chunk order,
+// then visit node slots 0..NN-1 in slot order and fold in every ALLOWED slot
+// one at a time (score, online-softmax update, acc += p*v, all fp32). Masked
+// slots are skipped, which is exactly what the reference's -inf scores do
+// (exp(-inf) = 0, alpha = 1), so a row's result depends only on the values of
+// its allowed keys and their order, never on where siblings sit in the buffer
+// or on how many rows the call carries. Final acc / l, one cast.
+#include "attention.cuh"
+#include "common.cuh"
+#include "host_util.h"
+
+namespace rb {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <typename T> __device__ __forceinline__ float ldf(const T* p);
+template <> __device__ __forceinline__ float ldf<float>(const float* p) { return *p; }
+template <> __device__ __forceinline__ float ldf<uint16_t>(const uint16_t* p) { return bf16_bits_to_f32(*p); }
+
+// Loads 4 consecutive elements as fp32.
+template <typename T> __device__ __forceinline__ void ld4(const T* p, float (&v)[4]);
+template <> __device__ __forceinline__ void ld4<float>(const float* p, float (&v)[4]) {
+  const float4 t = *reinterpret_cast<const float4*>(p);
+  v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+}
+template <> __device__ __forceinline__ void ld4<uint16_t>(const uint16_t* p, float (&v)[4]) {
+  const uint2 t = *reinterpret_cast<const uint2*>(p);
+  v[0] = bf16_bits_to_f32(static_cast<uint16_t>(t.x));
+  v[1] = bf16_bits_to_f32(static_cast<uint16_t>(t.x >> 16));
+  v[2] = bf16_bits_to_f32(static_cast<uint16_t>(t.y));
+  v[3] = bf16_bits_to_f32(static_cast<uint16_t>(t.y >> 16));
+}
+
+// ----------------------------------------------------------------- prefix (SIMT)
+// Block = 4 warps = 16 query rows of one head over one prefix chunk. Key tiles
+// of 32 staged in shared memory; lane j scores key j of the tile.
+template <typename T>
+__global__ void __launch_bounds__(128) attn_prefix_simt(const AttnDev p, float* __restrict__ part, int nchunks) {
+  constexpr int D = 128, TK = 32, RB = 16;
+  __shared__ float ks[TK][D + 1];
+  __shared__ __align__(16) float vs[TK][D];
+  __shared__ __align__(16) float qs[RB][D];
+  const int c = blockIdx.x, h = blockIdx.y, r0 = blockIdx.z * RB;
+  const int kvh = h / (p.H / p.HK);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NP = p.sp ? p.sp->prompt_len : p.NP;
+  const int M = p.sp ? min(p.M, p.sp->q) : p.M;
+  const int k0 = c * kPrefixChunk;
+  const int k1 = min(NP, k0 + kPrefixChunk);
+  if (k0 >= k1 || r0 >= M) return;  // chunk beyond the prefix / rows beyond the live ones
+  const T* q = static_cast<const T*>(p.q);
+  const T* kp = static_cast<const T*>(p.kp);
+  const T* vp = static_cast<const T*>(p.vp);
+
+  for (int i = threadIdx.x; i < RB * D; i += blockDim.x) {
+    const int r = i / D, d = i % D;
+    qs[r][d] = (r0 + r < M) ? ldf(q + h * p.sqh + static_cast<int64_t>(r0 + r) * p.sqm + d) : 0.f;
+  }
+  float m[4], l[4], acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -INFINITY; l[i] = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
+  }
+  const float scale2 = p.sm_scale * kLog2e;
+  for (int kt = k0; kt < k1; kt += TK) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < TK * D / 4; i += blockDim.x) {
+      const int j = i / (D / 4), d4 = (i % (D / 4)) * 4;
+      float kv[4] = {0.f, 0.f, 0.f, 0.f}, vv[4] = {0.f, 0.f, 0.f, 0.f};
+      if (kt + j < k1) {
+        ld4(kp + kvh * p.skph + static_cast<int64_t>(kt + j) * p.skpn + d4, kv);
+        ld4(vp + kvh * p.svph + static_cast<int64_t>(kt + j) * p.svpn + d4, vv);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) { ks[j][d4 + e] = kv[e]; vs[j][d4 + e] = vv[e]; }
+    }
+    __syncthreads();
+    const bool kvalid = kt + lane < k1;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = warp * 4 + i;
+      float s = 0.f;
+#pragma unroll 8
+      for (int d = 0; d < D; ++d) s = fmaf(qs[r][d], ks[lane][d], s);
+      s = kvalid ? s * scale2 : -INFINITY;
+      const float tmax = warp_max(s);
+      const float m_new = fmaxf(m[i], tmax);
+      const float alpha = fast_exp2(m[i] - m_new);
+      const float pj = fast_exp2(s - m_new);
+      float psum = warp_sum(pj);
+      psum = __shfl_sync(0xffffffffu, psum, 0);
+      // bf16 inputs: the probabilities enter the value product as bf16 (attention.py:48).
+      const float pv = sizeof(T) == 2 ? round_bf16(pj) : pj;
+      float t[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+      for (int j = 0; j < TK; ++j) {
+        const float pb = __shfl_sync(0xffffffffu, pv, j);
+        const float4 v4 = *reinterpret_cast<const float4*>(&vs[j][lane * 4]);
+        t[0] = fmaf(pb, v4.x, t[0]); t[1] = fmaf(pb, v4.y, t[1]);
+        t[2] = fmaf(pb, v4.z, t[2]); t[3] = fmaf(pb, v4.w, t[3]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[i][e] = fmaf(acc[i][e], alpha, t[e]);
+      l[i] = fmaf(l[i], alpha, psum);
+      m[i] = m_new;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = r0 + warp * 4 + i;
+    if (r >= M) continue;
+    float* o = part + ((static_cast<int64_t>(c) * p.H + h) * p.M + r) * kPartStride;
+    *reinterpret_cast<float4*>(o + lane * 4) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+    if (lane == 0) { o[D] = m[i]; o[D + 1] = l[i]; }
+  }
+}
+
+// ----------------------------------------------------------------- node phase
+__device__ __forceinline__ bool node_allowed(const AttnDev& p, int row, int j) {
+  switch (p.mask_kind) {
+    case RB_MASK_BOOL:
+      return static_cast<const uint8_t*>(p.msk)[row * p.smm + j * p.smn] != 0;
+    case RB_MASK_ADD_BF16:
+      return (static_cast<const uint16_t*>(p.msk)[row * p.smm + j * p.smn] & 0x7FFFu) == 0;
+    case RB_MASK_ADD_F32:
+      return static_cast<const float*>(p.msk)[row * p.smm + j * p.smn] == 0.f;
+    default:
+      return j <= row + p.causal_first;
+  }
+}
+
+// Fold node slot j into (m, l, acc): score by a fixed warp tree (every lane
+// takes lane 0's sum), then the online-softmax update, all fp32. This is the
+// only place node slots enter a row, whatever the masking mode.
+template <typename T>
+__device__ __forceinline__ void fold_node(const AttnDev& p, const T* kn, const T* vn, int kvh, int j,
+                                          const float (&qv)[4], int d0, float scale2, float& m, float& l,
+                                          float (&acc)[4]) {
+  float kv[4], vv[4];
+  ld4(kn + kvh * p.sknh + static_cast<int64_t>(j) * p.sknn + d0, kv);
+  ld4(vn + kvh * p.svnh + static_cast<int64_t>(j) * p.svnn + d0, vv);
+  float s = qv[0] * kv[0];
+  s = fmaf(qv[1], kv[1], s);
+  s = fmaf(qv[2], kv[2], s);
+  s = fmaf(qv[3], kv[3], s);
+  s = warp_sum(s);
+  s = __shfl_sync(0xffffffffu, s, 0) * scale2;
+  const float m_new = fmaxf(m, s);
+  const float a = fast_exp2(m - m_new);
+  const float pe = fast_exp2(s - m_new);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) acc[e] = fmaf(pe, vv[e], acc[e] * a);
+  l = fmaf(l, a, pe);
+  m = m_new;
+}
+
+constexpr int kMaxTrieDepth = 1024;
+
+// One warp per (head, query row); lane owns dims [4*lane, 4*lane+4).
+template <typename T>
+__global__ void __launch_bounds__(128) attn_nodes(const AttnDev p, const float* __restrict__ part) {
+  constexpr int D = 128;
+  __shared__ int chain[4][kMaxTrieDepth];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 4 + warp;
+  const int h = blockIdx.y;
+  if (row >= p.M) return;
+  const int d0 = lane * 4;
+  T* out = static_cast<T*>(p.out) + h * p.soh + static_cast<int64_t>(row) * p.som + d0;
+  const int live = p.sp ? p.sp->q : p.M;
+  if (row >= live) {  // padding row of a bucketed engine step: zeros, no reads
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (sizeof(T) == 2) reinterpret_cast<uint16_t*>(out)[e] = 0;
+      else reinterpret_cast<float*>(out)[e] = 0.f;
+    }
+    return;
+  }
+  const int NP = p.sp ? p.sp->prompt_len : p.NP;
+  const int nchunks = (NP + kPrefixChunk - 1) / kPrefixChunk;
+  const int kvh = h / (p.H / p.HK);
+  const T* q = static_cast<const T*>(p.q);
+  // Node slot 0 sits right after the prefix; without explicit node tensors
+  // (engine path) the node segment is the same buffer from key NP on.
+  const T* kn = p.kn ? static_cast<const T*>(p.kn) : static_cast<const T*>(p.kp) + static_cast<int64_t>(NP) * p.skpn;
+  const T* vn = p.vn ? static_cast<const T*>(p.vn) : static_cast<const T*>(p.vp) + static_cast<int64_t>(NP) * p.svpn;
+  float qv[4];
+  ld4(q + h * p.sqh + static_cast<int64_t>(row) * p.sqm + d0, qv);
+
+  // Merge prefix chunks in ascending chunk order.
+  float m = -INFINITY, l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int c = 0; c < nchunks; ++c) {
+    const float* o = part + ((static_cast<int64_t>(c) * p.H + h) * p.M + row) * kPartStride;
+    const float mc = o[D];
+    if (mc == -INFINITY) continue;
+    const float lc = o[D + 1];
+    const float4 ac = *reinterpret_cast<const float4*>(o + d0);
+    const float m_new = fmaxf(m, mc);
+    const float a = fast_exp2(m - m_new);
+    const float b = fast_exp2(mc - m_new);
+    acc[0] = fmaf(ac.x, b, acc[0] * a); acc[1] = fmaf(ac.y, b, acc[1] * a);
+    acc[2] = fmaf(ac.z, b, acc[2] * a); acc[3] = fmaf(ac.w, b, acc[3] * a);
+    l = fmaf(lc, b, l * a);
+    m = m_new;
+  }
+
+  const float scale2 = p.sm_scale * kLog2e;
+  if (p.mask_kind == kMaskTrie) {
+    // Committed slots, in order, then the ancestors-or-self of this node in
+    // increasing index (= slot) order; every other slot is masked.
+    const int base = p.sp ? p.sp->base : p.causal_first;
+    for (int j = 0; j < base; ++j) fold_node<T>(p, kn, vn, kvh, j, qv, d0, scale2, m, l, acc);
+    int depth = p.depths[row];
+    if (depth < 0 || depth >= kMaxTrieDepth) {
+      raise_device_error(0x201);
+      depth = -1;
+    }
+    if (lane == 0) {
+      int a = row;
+      for (int t = depth; t >= 0; --t) {
+        chain[warp][t] = a;
+        const int par = p.parents[a];
+        if ((t > 0 && (par < 0 || par >= a)) || (t == 0 && par != -1)) {
+          raise_device_error(0x202);  // parents / depths inconsistent: fold nothing more
+          depth = -1;
+          break;
+        }
+        a = par;
+      }
+    }
+    depth = __shfl_sync(0xffffffffu, depth, 0);
+    __syncwarp();
+    for (int t = 0; t <= depth; ++t) fold_node<T>(p, kn, vn, kvh, base + chain[warp][t], qv, d0, scale2, m, l, acc);
+  } else {
+    // Node slots in slot order, allowed ones only (a masked slot is an exact no-op).
+    for (int j0 = 0; j0 < p.NN; j0 += 32) {
+      const int j = j0 + lane;
+      const bool allow = j < p.NN && node_allowed(p, row, j);
+      unsigned bits = __ballot_sync(0xffffffffu, allow);
+      while (bits) {
+        const int jj = j0 + __ffs(bits) - 1;
+        bits &= bits - 1;
+        fold_node<T>(p, kn, vn, kvh, jj, qv, d0, scale2, m, l, acc);
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float v = __fdiv_rn(acc[e], l);
+    if (sizeof(T) == 2) reinterpret_cast<uint16_t*>(out)[e] = f32_to_bf16_bits(v);
+    else reinterpret_cast<float*>(out)[e] = v;
+  }
+}
+
+// ----------------------------------------------------------------- host
+size_t attn_workspace_bytes(int H, int M, int D, int NP) {
+  (void)D;
+  const int nchunks = (NP + kPrefixChunk - 1) / kPrefixChunk;
+  return static_cast<size_t>(nchunks > 0 ? nchunks : 1) * H * (M > 0 ? M : 1) * kPartStride * sizeof(float);
+}
+
+int attn_validate(const rb_attn_args* a) {
+  if (!a) return RB_ERR_INVALID_ARG;
+  if (a->dtype != RB_F32 && a->dtype != RB_BF16) return RB_ERR_UNSUPPORTED;
+  if (a->H <= 0 || a->HK <= 0 || a->M < 0 || a->NP < 0 || a->NN < 0) return RB_ERR_INVALID_ARG;
+  if (a->H % a->HK != 0) return RB_ERR_INVALID_ARG;
+  if (a->D != 128) return RB_ERR_UNSUPPORTED;
+  if (a->sqd != 1 || a->skpd != 1 || a->svpd != 1 || a->sknd != 1 || a->svnd != 1 || a->sod != 1)
+    return RB_ERR_UNSUPPORTED;
+  if (!a->q || !a->out || (a->NP > 0 && (!a->kp || !a->vp)) || (a->NN > 0 && (!a->kn || !a->vn)))
+    return RB_ERR_INVALID_ARG;
+  if (a->mask_kind < RB_MASK_BOOL || a->mask_kind > RB_MASK_CAUSAL) return RB_ERR_INVALID_ARG;
+  if (a->mask_kind != RB_MASK_CAUSAL && a->NN > 0 && !a->msk) return RB_ERR_INVALID_ARG;
+  // Vector loads of 4 elements need 4-element-aligned row strides and bases.
+  const int64_t strides[] = {a->sqh, a->sqm, a->skph, a->skpn, a->svph, a->svpn,
+                             a->sknh, a->sknn, a->svnh, a->svnn, a->soh, a->som};
+  for (int64_t s : strides)
+    if (s % 4 != 0) return RB_ERR_UNSUPPORTED;
+  const int eb = a->dtype == RB_F32 ? 4 : 2;
+  const void* ptrs[] = {a->q, a->kp, a->vp, a->kn, a->vn, a->out};
+  for (const void* ptr : ptrs)
+    if (ptr && (reinterpret_cast<uintptr_t>(ptr) % (4 * eb)) != 0) return RB_ERR_UNSUPPORTED;
+  return RB_OK;
+}
+
+int attn_launch(const rb_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  const int st = attn_validate(a);
+  if (st != RB_OK) return st;
+  if (a->M == 0) return RB_OK;
+  const size_t need = attn_workspace_bytes(a->H, a->M, a->D, a->NP);
+  if (!ws || ws_bytes < need) return RB_ERR_WORKSPACE;
+  AttnDev p{};
+  p.H = a->H; p.M = a->M; p.HK = a->HK; p.NP = a->NP; p.NN = a->NN;
+  p.q = a->q; p.sqh = a->sqh; p.sqm = a->sqm;
+  p.kp = a->kp; p.skph = a->skph; p.skpn = a->skpn;
+  p.vp = a->vp; p.svph = a->svph; p.svpn = a->svpn;
+  p.kn = a->kn; p.sknh = a->sknh; p.sknn = a->sknn;
+  p.vn = a->vn; p.svnh = a->svnh; p.svnn = a->svnn;
+  p.msk = a->msk; p.mask_kind = a->mask_kind; p.smm = a->smm; p.smn = a->smn;
+  p.causal_first = a->causal_first;
+  p.out = a->out; p.soh = a->soh; p.som = a->som;
+  p.sm_scale = a->sm_scale;
+  float* part = static_cast<float*>(ws);
+  const int nchunks = (a->NP + kPrefixChunk - 1) / kPrefixChunk;
+  if (nchunks > 0) {
+    dim3 grid(nchunks, a->H, (a->M + 15) / 16);
+    if (a->dtype == RB_F32) attn_prefix_simt<float><<<grid, 128, 0, stream>>>(p, part, nchunks);
+    else attn_prefix_simt<uint16_t><<<grid, 128, 0, stream>>>(p, part, nchunks);
+    if (cudaGetLastError() != cudaSuccess) return RB_ERR_CUDA;
+  }
+  dim3 grid2((a->M + 3) / 4, a->H);
+  if (a->dtype == RB_F32) attn_nodes<float><<<grid2, 128, 0, stream>>>(p, part);
+  else attn_nodes<uint16_t><<<grid2, 128, 0, stream>>>(p, part);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;
+}
+
+// Engine path: bf16, q/base/PL from device memory, trie masking from parents.
+int attn_launch_engine(const AttnDev& p, float* part, int max_chunks, cudaStream_t stream) {
+  dim3 grid(max_chunks, p.H, (p.M + 15) / 16);
+  attn_prefix_simt<uint16_t><<<grid, 128, 0, stream>>>(p, part, max_chunks);
+  if (cudaGetLastError() != cudaSuccess) return RB_ERR_CUDA;
+  dim3 grid2((p.M + 3) / 4, p.H);
+  attn_nodes<uint16_t><<<grid2, 128, 0, stream>>>(p, part);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;
+}
+
+}  // namespace rb

@@ -1,0 +1,53 @@
+// Trie-verification attention: device parameter block and launchers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/respect_b200.h"
+
+namespace rb {
+
+// Prefix keys are reduced in chunks of this many keys at absolute positions
+// [c*kPrefixChunk, (c+1)*kPrefixChunk). A compile-time constant: results of a
+// row depend on it, so it must never vary with the call.
+constexpr int kPrefixChunk = 512;
+// Per (chunk, head, row) partial: acc[128], max (log2 domain), sum, 2 pad.
+constexpr int kPartStride = 128 + 4;
+
+// Step values an engine graph reads from device memory at run time, so that
+// one captured graph serves every (rows <= bucket, committed, prompt length).
+struct StepParams {
+  int q;           // live query rows (trie nodes)
+  int base;        // committed tokens after the prompt
+  int prompt_len;  // PL: keys [0, PL) are the prefix
+  int rope_delta;  // added to every rotary position (verify.py:31)
+  int act_off, act_size;  // excluded vocabulary range of the greedy choice
+  int pad[2];
+};
+
+// Node masking modes beyond the public rb_mask_kind values.
+constexpr int kMaskTrie = 16;  // committed slots [0, base) then the row's ancestors, from parents[]
+
+struct AttnDev {
+  int H, M, HK, NP, NN;
+  const StepParams* sp;       // non-null: q, base and NP come from device memory
+  const int32_t* parents;     // kMaskTrie
+  const int32_t* depths;      // kMaskTrie
+  const void* q; int64_t sqh, sqm;
+  const void* kp; int64_t skph, skpn;
+  const void* vp; int64_t svph, svpn;
+  const void* kn; int64_t sknh, sknn;
+  const void* vn; int64_t svnh, svnn;
+  const void* msk; int mask_kind; int64_t smm, smn;
+  int causal_first;
+  void* out; int64_t soh, som;
+  float sm_scale;
+};
+
+size_t attn_workspace_bytes(int H, int M, int D, int NP);
+int attn_validate(const rb_attn_args* a);
+int attn_launch(const rb_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t stream);
+int attn_launch_engine(const AttnDev& p, float* part, int max_chunks, cudaStream_t stream);
+
+}  // namespace rb

@@ -1,0 +1,618 @@
+// Native verify-step engine: one forward of a Qwen3-style decoder over the
+// nodes of a trie, with the dedicated kernels, as respect/decoding/verify.py:12-46
+// runs it through HF with respect/kernels/patch.py:70-107 installed.
+//
+// Per layer (HF Qwen3VLTextDecoderLayer order, PyTorch rounding points):
+//   xn = rmsnorm(h)                       (fused into the previous finish kernel)
+//   qkv = xn @ Wqkv^T                     split-K tcgen05 GEMM -> fp32 partials
+//   q,k = rope(rmsnorm_head(bf16 qkv))    qkv_finish: fixed-order split sum, per-head
+//   v   = bf16 qkv                        norm, RoPE, K/V written to their slots
+//   a   = trie attention                  prefix chunks + committed + ancestors
+//   h   = bf16(h + bf16(a @ Wo^T))        o GEMM + resid_finish (+ post-attn norm)
+//   act = silu(bf16 g) * bf16 u           gate/up GEMM with the SiLU*mul epilogue
+//   h   = bf16(h + bf16(act @ Wd^T))      down GEMM + resid_finish (+ next norm)
+// then logits = final_norm(h) @ Wlm^T in fp32 and the greedy choice per row.
+//
+// Every reduction has an order fixed by the shapes alone, and each fused
+// kernel uses the reduction structure of the standalone operator it replaces,
+// so an engine step is bitwise equal to composing rb_linear / rb_rmsnorm /
+// rb_rope / rb_silu_mul / rb_fused_attn_hyb, and a row's results never depend
+// on how many rows the step carries.
+#include <map>
+#include <vector>
+
+#include "attention.cuh"
+#include "common.cuh"
+#include "elementwise.cuh"
+#include "gemm.cuh"
+#include "host_util.h"
+
+namespace rb {
+
+// ------------------------------------------------------------------ kernels
+// Row RMSNorm pieces shared with rmsnorm_kernel (elementwise.cu): thread t of
+// NT owns elements t, t+NT, ...; fmaf chain in that order, warp tree, lane-0
+// broadcast, warps summed in ascending order.
+template <int NT>
+__device__ __forceinline__ float row_inv_rms(const float* v, int cnt, int N, float eps, float* red) {
+  float ss = 0.f;
+  for (int k = 0; k < cnt; ++k) ss = fmaf(v[k], v[k], ss);
+  ss = warp_sum(ss);
+  ss = __shfl_sync(0xffffffffu, ss, 0);
+  const int t = threadIdx.x;
+  if ((t & 31) == 0) red[t >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) tot += red[i];
+  return rsqrtf(tot / static_cast<float>(N) + eps);
+}
+
+constexpr int kMaxPerThread = 32;  // hidden <= 32 * NT
+
+// h[row] = embed[ids[row]];  xn[row] = rmsnorm(h[row], w)
+template <int NT>
+__global__ void __launch_bounds__(NT) embed_norm_kernel(const StepParams* __restrict__ sp, const int32_t* __restrict__ ids,
+                                                        const uint16_t* __restrict__ emb, const uint16_t* __restrict__ w,
+                                                        uint16_t* __restrict__ h, uint16_t* __restrict__ xn, int N,
+                                                        int vocab, float eps) {
+  __shared__ float red[NT / 32];
+  const int row = blockIdx.x;
+  if (row >= sp->q) return;
+  int id = ids[row];
+  if (id < 0 || id >= vocab) {
+    raise_device_error(0x301);
+    id = 0;
+  }
+  const uint16_t* er = emb + static_cast<int64_t>(id) * N;
+  float v[kMaxPerThread];
+  int cnt = 0;
+  for (int i = threadIdx.x; i < N; i += NT) {
+    const uint16_t b = er[i];
+    h[static_cast<int64_t>(row) * N + i] = b;
+    v[cnt++] = bf16_bits_to_f32(b);
+  }
+  const float r = row_inv_rms<NT>(v, cnt, N, eps, red);
+  cnt = 0;
+  for (int i = threadIdx.x; i < N; i += NT) {
+    const float xh = round_bf16(v[cnt++] * r);
+    xn[static_cast<int64_t>(row) * N + i] = f32_to_bf16_bits(bf16_bits_to_f32(w[i]) * xh);
+  }
+}
+
+// o = bf16(sum_s partial[s]);  h = bf16(h + o);  xn = rmsnorm(h, w)
+template <int NT>
+__global__ void __launch_bounds__(NT) resid_norm_kernel(const StepParams* __restrict__ sp, const float* __restrict__ part,
+                                                        int splits, int M, uint16_t* __restrict__ h,
+                                                        const uint16_t* __restrict__ w, uint16_t* __restrict__ xn, int N,
+                                                        float eps) {
+  __shared__ float red[NT / 32];
+  const int row = blockIdx.x;
+  if (row >= sp->q) return;
+  const int64_t plane = static_cast<int64_t>(M) * N;
+  float v[kMaxPerThread];
+  int cnt = 0;
+  for (int i = threadIdx.x; i < N; i += NT) {
+    const float* p = part + static_cast<int64_t>(row) * N + i;
+    float acc = p[0];
+    for (int s = 1; s < splits; ++s) acc += p[s * plane];
+    const float o = round_bf16(acc);
+    const int64_t idx = static_cast<int64_t>(row) * N + i;
+    const float hn = round_bf16(bf16_bits_to_f32(h[idx]) + o);
+    h[idx] = f32_to_bf16_bits(hn);
+    v[cnt++] = hn;
+  }
+  const float r = row_inv_rms<NT>(v, cnt, N, eps, red);
+  cnt = 0;
+  for (int i = threadIdx.x; i < N; i += NT) {
+    const float xh = round_bf16(v[cnt++] * r);
+    xn[static_cast<int64_t>(row) * N + i] = f32_to_bf16_bits(bf16_bits_to_f32(w[i]) * xh);
+  }
+}
+
+// One warp per (row, head) of the fused q|k|v projection output (D = 128,
+// lane owns d = lane + 32k). q/k heads: per-head RMSNorm with the reduction of
+// rmsnorm_kernel<NT=32>, then RoPE at the node's rotary position; v: copy.
+__global__ void __launch_bounds__(128) qkv_finish_kernel(
+    const StepParams* __restrict__ sp, const int32_t* __restrict__ depths, const float* __restrict__ part,
+    int splits, int M, int H, int HK, const uint16_t* __restrict__ qn_w, const uint16_t* __restrict__ kn_w,
+    const uint16_t* __restrict__ cos_t, const uint16_t* __restrict__ sin_t, int max_pos, float eps,
+    uint16_t* __restrict__ qbuf, uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, int64_t kv_s_head,
+    int max_slots) {
+  constexpr int D = 128;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x;
+  const int head = blockIdx.y * 4 + warp;
+  const int nh = H + 2 * HK;
+  if (row >= sp->q || head >= nh) return;
+  const int N = nh * D;
+  const int64_t plane = static_cast<int64_t>(M) * N;
+  float x[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float* p = part + static_cast<int64_t>(row) * N + head * D + lane + 32 * k;
+    float acc = p[0];
+    for (int s = 1; s < splits; ++s) acc += p[s * plane];
+    x[k] = round_bf16(acc);
+  }
+  const int slot = sp->prompt_len + sp->base + row;
+  if (slot >= max_slots) {
+    raise_device_error(0x302);
+    return;
+  }
+  if (head >= H + HK) {  // v head
+    uint16_t* dst = vc + (head - H - HK) * kv_s_head + static_cast<int64_t>(slot) * D;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = f32_to_bf16_bits(x[k]);
+    return;
+  }
+  const uint16_t* w = head < H ? qn_w : kn_w;
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) ss = fmaf(x[k], x[k], ss);
+  ss = warp_sum(ss);
+  ss = __shfl_sync(0xffffffffu, ss, 0);
+  const float r = rsqrtf((0.f + ss) / static_cast<float>(D) + eps);
+  float y[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) y[k] = round_bf16(bf16_bits_to_f32(w[lane + 32 * k]) * round_bf16(x[k] * r));
+  int pos = sp->prompt_len + sp->base + depths[row] + sp->rope_delta;
+  if (pos < 0 || pos >= max_pos) {
+    raise_device_error(0x303);
+    pos = 0;
+  }
+  const uint16_t* cr = cos_t + static_cast<int64_t>(pos) * D;
+  const uint16_t* sr = sin_t + static_cast<int64_t>(pos) * D;
+  float o[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int d = lane + 32 * k;
+    const float xr = k < 2 ? -y[k + 2] : y[k - 2];  // rotate_half: d < 64 takes -x[d+64]
+    const float a = round_bf16(__fmul_rn(y[k], bf16_bits_to_f32(cr[d])));
+    const float b = round_bf16(__fmul_rn(xr, bf16_bits_to_f32(sr[d])));
+    o[k] = round_bf16(__fadd_rn(a, b));
+  }
+  uint16_t* dst;
+  if (head < H) dst = qbuf + (static_cast<int64_t>(head) * M + row) * D;
+  else dst = kc + (head - H) * kv_s_head + static_cast<int64_t>(slot) * D;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = f32_to_bf16_bits(o[k]);
+}
+
+// Greedy choice of the live rows, reading the excluded range from the params.
+__global__ void greedy_step_kernel(const StepParams* __restrict__ sp, const float* __restrict__ logits, int64_t ld,
+                                   int V, int64_t* __restrict__ out) {
+  const int row = blockIdx.x;
+  if (row >= sp->q) return;
+  const float* r = logits + static_cast<int64_t>(row) * ld;
+  const int off = sp->act_off, size = sp->act_size;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    if (i >= off && i < off + size) continue;
+    const float v = r[i];
+    if (better(v, i, bv, bi)) { bv = v; bi = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+      if (better(sv[w], si[w], bv, bi)) { bv = sv[w]; bi = si[w]; }
+    out[row] = (bi == 0x7fffffff) ? 0 : bi;
+  }
+}
+
+}  // namespace rb
+
+// ------------------------------------------------------------------ host engine
+using namespace rb;
+
+struct rb_engine {
+  rb_model_config cfg;
+  rb_model_weights w;
+  std::vector<rb_layer_weights> layers;
+  std::vector<void*> kc, vc;
+  int dev = 0;
+  int nsm = 148;
+  // workspace carve-up
+  StepParams* d_params = nullptr;
+  int32_t *d_ids = nullptr, *d_parents = nullptr, *d_depths = nullptr;
+  int64_t* d_out = nullptr;
+  uint16_t *h = nullptr, *xn = nullptr, *qbuf = nullptr, *attn = nullptr, *act = nullptr;
+  float *part = nullptr, *apart = nullptr, *logits = nullptr;
+  int max_chunks = 1;
+  // tensor maps
+  CUtensorMap m_xn, m_attn, m_act, m_lm;
+  std::vector<CUtensorMap> m_qkv, m_o, m_gu, m_d;
+  int bn_lm = 256;
+  // host staging and graphs
+  uint8_t* pinned = nullptr;
+  size_t pinned_bytes = 0;
+  cudaEvent_t staged = nullptr;
+  bool staged_pending = false;
+  cudaStream_t cap = nullptr;
+  std::map<int, cudaGraphExec_t> graphs;
+  std::map<int, cudaGraph_t> graph_defs;
+};
+
+namespace {
+
+constexpr int kQkvNT = 128;
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Layout {
+  size_t params, ids, parents, depths, out, h, xn, qbuf, attn, act, part, apart, logits, total;
+};
+
+Layout layout_of(const rb_model_config& c) {
+  Layout L{};
+  const size_t R = static_cast<size_t>(c.max_rows);
+  const int nsm = device_sm_count();
+  const int nqkv = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
+  const GemmShape s_qkv = gemm_plan(c.max_rows, nqkv, c.hidden, nsm);
+  const GemmShape s_o = gemm_plan(c.max_rows, c.hidden, c.n_heads * c.head_dim, nsm);
+  const GemmShape s_d = gemm_plan(c.max_rows, c.hidden, c.ffn, nsm);
+  size_t part_elems = static_cast<size_t>(s_qkv.splits) * nqkv;
+  part_elems = std::max(part_elems, static_cast<size_t>(s_o.splits) * c.hidden);
+  part_elems = std::max(part_elems, static_cast<size_t>(s_d.splits) * c.hidden);
+  const int max_chunks = (c.max_slots + kPrefixChunk - 1) / kPrefixChunk;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { const size_t o = off; off = align256(off + bytes); return o; };
+  L.params = take(sizeof(StepParams));
+  L.ids = take(R * 4);
+  L.parents = take(R * 4);
+  L.depths = take(R * 4);
+  L.out = take(R * 8);
+  L.h = take(R * c.hidden * 2);
+  L.xn = take(R * c.hidden * 2);
+  L.qbuf = take(static_cast<size_t>(c.n_heads) * R * c.head_dim * 2);
+  L.attn = take(R * c.n_heads * c.head_dim * 2);
+  L.act = take(R * c.ffn * 2);
+  L.part = take(part_elems * R * 4);
+  L.apart = take(static_cast<size_t>(max_chunks) * c.n_heads * R * kPartStride * 4);
+  L.logits = take(R * c.vocab * 4);
+  L.total = off;
+  return L;
+}
+
+int validate_cfg(const rb_model_config* c) {
+  if (!c) return RB_ERR_INVALID_ARG;
+  if (c->hidden <= 0 || c->n_layers <= 0 || c->n_heads <= 0 || c->n_kv_heads <= 0 || c->ffn <= 0 ||
+      c->vocab <= 0 || c->max_rows <= 0 || c->max_slots <= 0 || c->max_pos <= 0)
+    return RB_ERR_INVALID_ARG;
+  if (c->head_dim != 128 || c->n_heads % c->n_kv_heads != 0) return RB_ERR_UNSUPPORTED;
+  if (c->hidden % 64 != 0 || c->ffn % 128 != 0 || c->vocab % 8 != 0) return RB_ERR_UNSUPPORTED;
+  if (c->hidden > kMaxPerThread * 256) return RB_ERR_UNSUPPORTED;
+  if (c->max_rows > 1024 || c->n_layers > RB_COMPACT_MAX_LAYERS) return RB_ERR_CAPACITY;
+  return RB_OK;
+}
+
+template <typename F>
+int launch_norm_nt(int N, F&& f) {
+  if (N >= 2048) return f(std::integral_constant<int, 256>{});
+  if (N >= 512) return f(std::integral_constant<int, 128>{});
+  return f(std::integral_constant<int, 32>{});
+}
+
+#define RB_TRY(x)                     \
+  do {                                \
+    const int _st = (x);              \
+    if (_st != RB_OK) return _st;     \
+  } while (0)
+
+int check_launch() { return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA; }
+
+// Enqueue one verify step for `rows` (bucketed) query rows on `st`.
+int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
+  const rb_model_config& c = e->cfg;
+  const int H = c.n_heads, HK = c.n_kv_heads, D = c.head_dim;
+  const int nqkv = (H + 2 * HK) * D;
+  const int hid = c.hidden;
+  const GemmShape s_qkv = gemm_plan(rows, nqkv, hid, e->nsm);
+  const GemmShape s_o = gemm_plan(rows, hid, H * D, e->nsm);
+  const GemmShape s_gu = gemm_plan(rows, 2 * c.ffn, hid, e->nsm, 256, 1);
+  const GemmShape s_d = gemm_plan(rows, hid, c.ffn, e->nsm);
+  const GemmShape s_lm = gemm_plan(rows, c.vocab, hid, e->nsm);
+  if (s_lm.BN != e->bn_lm) return RB_ERR_INVALID_ARG;
+
+  RB_TRY(launch_norm_nt(hid, [&](auto nt) {
+    constexpr int NT = decltype(nt)::value;
+    embed_norm_kernel<NT><<<rows, NT, 0, st>>>(e->d_params, e->d_ids, static_cast<const uint16_t*>(e->w.embed),
+                                               static_cast<const uint16_t*>(e->layers[0].in_norm), e->h, e->xn, hid,
+                                               c.vocab, c.rms_eps);
+    return check_launch();
+  }));
+  for (int l = 0; l < c.n_layers; ++l) {
+    const rb_layer_weights& lw = e->layers[l];
+    GemmLaunch g{};
+    // q|k|v projection
+    g.epi = kEpiPartial;
+    g.partial = e->part;
+    RB_TRY(gemm_launch_maps(s_qkv, e->m_xn, e->m_qkv[l], g, st));
+    dim3 gq(rows, (H + 2 * HK + 3) / 4);
+    qkv_finish_kernel<<<gq, kQkvNT, 0, st>>>(
+        e->d_params, e->d_depths, e->part, s_qkv.splits, rows, H, HK, static_cast<const uint16_t*>(lw.q_norm),
+        static_cast<const uint16_t*>(lw.k_norm), static_cast<const uint16_t*>(e->w.rope_cos),
+        static_cast<const uint16_t*>(e->w.rope_sin), c.max_pos, c.rms_eps, e->qbuf,
+        static_cast<uint16_t*>(e->kc[l]), static_cast<uint16_t*>(e->vc[l]),
+        static_cast<int64_t>(c.max_slots) * D, c.max_slots);
+    RB_TRY(check_launch());
+    // attention over [prefix | committed | trie]
+    AttnDev p{};
+    p.H = H; p.M = rows; p.HK = HK; p.NP = 0; p.NN = 0;
+    p.sp = e->d_params;
+    p.parents = e->d_parents;
+    p.depths = e->d_depths;
+    p.q = e->qbuf; p.sqh = static_cast<int64_t>(rows) * D; p.sqm = D;
+    const int64_t sh = static_cast<int64_t>(c.max_slots) * D;
+    p.kp = e->kc[l]; p.skph = sh; p.skpn = D;
+    p.vp = e->vc[l]; p.svph = sh; p.svpn = D;
+    // node slots start at the prompt length, which only the device knows:
+    // kn/vn are set per step by the kernels from sp->prompt_len (see below).
+    p.kn = nullptr; p.vn = nullptr; p.sknh = sh; p.sknn = D; p.svnh = sh; p.svnn = D;
+    p.mask_kind = kMaskTrie;
+    p.out = e->attn; p.soh = D; p.som = static_cast<int64_t>(H) * D;
+    p.sm_scale = 1.0f / sqrtf(static_cast<float>(D));
+    RB_TRY(attn_launch_engine(p, e->apart, e->max_chunks, st));
+    // o projection + residual + post-attention norm
+    g.epi = kEpiPartial;
+    RB_TRY(gemm_launch_maps(s_o, e->m_attn, e->m_o[l], g, st));
+    RB_TRY(launch_norm_nt(hid, [&](auto nt) {
+      constexpr int NT = decltype(nt)::value;
+      resid_norm_kernel<NT><<<rows, NT, 0, st>>>(e->d_params, e->part, s_o.splits, rows, e->h,
+                                                 static_cast<const uint16_t*>(lw.post_norm), e->xn, hid, c.rms_eps);
+      return check_launch();
+    }));
+    // gate|up with the SiLU*mul epilogue
+    GemmLaunch gu{};
+    gu.epi = kEpiSiluMul;
+    gu.out = e->act;
+    gu.ldo = c.ffn;
+    RB_TRY(gemm_launch_maps(s_gu, e->m_xn, e->m_gu[l], gu, st));
+    // down + residual + next norm
+    g.epi = kEpiPartial;
+    RB_TRY(gemm_launch_maps(s_d, e->m_act, e->m_d[l], g, st));
+    const void* next_norm = (l + 1 < c.n_layers) ? e->layers[l + 1].in_norm : e->w.final_norm;
+    RB_TRY(launch_norm_nt(hid, [&](auto nt) {
+      constexpr int NT = decltype(nt)::value;
+      resid_norm_kernel<NT><<<rows, NT, 0, st>>>(e->d_params, e->part, s_d.splits, rows, e->h,
+                                                 static_cast<const uint16_t*>(next_norm), e->xn, hid, c.rms_eps);
+      return check_launch();
+    }));
+  }
+  GemmLaunch gl{};
+  gl.epi = kEpiStoreF32;
+  gl.out = e->logits;
+  gl.ldo = c.vocab;
+  RB_TRY(gemm_launch_maps(s_lm, e->m_xn, e->m_lm, gl, st));
+  greedy_step_kernel<<<rows, 1024, 0, st>>>(e->d_params, e->logits, c.vocab, c.vocab, e->d_out);
+  return check_launch();
+}
+
+int bucket_of(int q) {
+  int b = 1;
+  while (b < q) b <<= 1;
+  return b;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t rb_engine_workspace_bytes(const rb_model_config* cfg) {
+  if (validate_cfg(cfg) != RB_OK) return 0;
+  return layout_of(*cfg).total;
+}
+
+int rb_engine_create(const rb_model_config* cfg, const rb_model_weights* w, void* workspace, size_t ws_bytes,
+                     rb_engine** out) {
+  RB_TRY(validate_cfg(cfg));
+  if (!w || !out || !w->layers || !w->k_cache || !w->v_cache || !w->embed || !w->final_norm || !w->lm_head ||
+      !w->rope_cos || !w->rope_sin)
+    return RB_ERR_INVALID_ARG;
+  const Layout L = layout_of(*cfg);
+  if (!workspace || ws_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255)) return RB_ERR_WORKSPACE;
+  rb_engine* e = new rb_engine();
+  e->cfg = *cfg;
+  e->w = *w;
+  e->layers.assign(w->layers, w->layers + cfg->n_layers);
+  e->kc.assign(w->k_cache, w->k_cache + cfg->n_layers);
+  e->vc.assign(w->v_cache, w->v_cache + cfg->n_layers);
+  e->w.layers = nullptr;
+  e->w.k_cache = e->w.v_cache = nullptr;
+  cudaGetDevice(&e->dev);
+  e->nsm = device_sm_count();
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  e->d_params = reinterpret_cast<StepParams*>(base + L.params);
+  e->d_ids = reinterpret_cast<int32_t*>(base + L.ids);
+  e->d_parents = reinterpret_cast<int32_t*>(base + L.parents);
+  e->d_depths = reinterpret_cast<int32_t*>(base + L.depths);
+  e->d_out = reinterpret_cast<int64_t*>(base + L.out);
+  e->h = reinterpret_cast<uint16_t*>(base + L.h);
+  e->xn = reinterpret_cast<uint16_t*>(base + L.xn);
+  e->qbuf = reinterpret_cast<uint16_t*>(base + L.qbuf);
+  e->attn = reinterpret_cast<uint16_t*>(base + L.attn);
+  e->act = reinterpret_cast<uint16_t*>(base + L.act);
+  e->part = reinterpret_cast<float*>(base + L.part);
+  e->apart = reinterpret_cast<float*>(base + L.apart);
+  e->logits = reinterpret_cast<float*>(base + L.logits);
+  e->max_chunks = (cfg->max_slots + kPrefixChunk - 1) / kPrefixChunk;
+
+  const rb_model_config& c = *cfg;
+  const int nqkv = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
+  int st = RB_OK;
+  st |= gemm_encode_x(&e->m_xn, e->xn, c.max_rows, c.hidden, c.hidden);
+  st |= gemm_encode_x(&e->m_attn, e->attn, c.max_rows, c.n_heads * c.head_dim, c.n_heads * c.head_dim);
+  st |= gemm_encode_x(&e->m_act, e->act, c.max_rows, c.ffn, c.ffn);
+  const GemmShape s_qkv = gemm_plan(1, nqkv, c.hidden, e->nsm);
+  const GemmShape s_o = gemm_plan(1, c.hidden, c.n_heads * c.head_dim, e->nsm);
+  const GemmShape s_d = gemm_plan(1, c.hidden, c.ffn, e->nsm);
+  const GemmShape s_lm = gemm_plan(1, c.vocab, c.hidden, e->nsm);
+  e->bn_lm = s_lm.BN;
+  e->m_qkv.resize(c.n_layers);
+  e->m_o.resize(c.n_layers);
+  e->m_gu.resize(c.n_layers);
+  e->m_d.resize(c.n_layers);
+  for (int l = 0; l < c.n_layers && st == RB_OK; ++l) {
+    const rb_layer_weights& lw = e->layers[l];
+    if (!lw.wqkv || !lw.wo || !lw.wgu || !lw.wd || !lw.in_norm || !lw.post_norm || !lw.q_norm || !lw.k_norm ||
+        !e->kc[l] || !e->vc[l]) {
+      st = RB_ERR_INVALID_ARG;
+      break;
+    }
+    st |= gemm_encode_w(&e->m_qkv[l], lw.wqkv, nqkv, c.hidden, c.hidden, s_qkv.BN);
+    st |= gemm_encode_w(&e->m_o[l], lw.wo, c.hidden, c.n_heads * c.head_dim, c.n_heads * c.head_dim, s_o.BN);
+    st |= gemm_encode_w(&e->m_gu[l], lw.wgu, 2 * c.ffn, c.hidden, c.hidden, 256);
+    st |= gemm_encode_w(&e->m_d[l], lw.wd, c.hidden, c.ffn, c.ffn, s_d.BN);
+  }
+  if (st == RB_OK) st = gemm_encode_w(&e->m_lm, w->lm_head, c.vocab, c.hidden, c.hidden, s_lm.BN);
+  if (st != RB_OK) {
+    delete e;
+    return st != RB_ERR_INVALID_ARG ? RB_ERR_UNSUPPORTED : st;
+  }
+  e->pinned_bytes = sizeof(StepParams) + 3 * static_cast<size_t>(c.max_rows) * 4;
+  if (cudaMallocHost(&e->pinned, e->pinned_bytes) != cudaSuccess ||
+      cudaEventCreateWithFlags(&e->staged, cudaEventDisableTiming) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&e->cap, cudaStreamNonBlocking) != cudaSuccess) {
+    rb_engine_destroy(e);
+    return RB_ERR_CUDA;
+  }
+  *out = e;
+  return RB_OK;
+}
+
+int rb_engine_destroy(rb_engine* e) {
+  if (!e) return RB_OK;
+  for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& kv : e->graph_defs) cudaGraphDestroy(kv.second);
+  if (e->staged) cudaEventDestroy(e->staged);
+  if (e->cap) cudaStreamDestroy(e->cap);
+  if (e->pinned) cudaFreeHost(e->pinned);
+  delete e;
+  return RB_OK;
+}
+
+int rb_engine_step(rb_engine* e, const rb_step_desc* d, void* stream) {
+  if (!e || !d) return RB_ERR_INVALID_ARG;
+  const rb_model_config& c = e->cfg;
+  if (d->q <= 0 || d->base < 0 || d->prompt_len < 0 || !d->ids || !d->parents || !d->depths)
+    return RB_ERR_INVALID_ARG;
+  if (d->q > c.max_rows) return RB_ERR_CAPACITY;
+  if (static_cast<int64_t>(d->prompt_len) + d->base + d->q > c.max_slots) return RB_ERR_CAPACITY;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  StepParams sp{};
+  sp.q = d->q;
+  sp.base = d->base;
+  sp.prompt_len = d->prompt_len;
+  sp.rope_delta = d->rope_delta;
+  sp.act_off = d->act_off;
+  sp.act_size = d->act_size;
+  const size_t n4 = static_cast<size_t>(d->q) * 4;
+  if (d->host_inputs) {
+    // Validate the trie on the host (parents precede children, depth = parent + 1).
+    for (int i = 0; i < d->q; ++i) {
+      const int p = d->parents[i];
+      if (p >= i || p < -1) return RB_ERR_INVALID_ARG;
+      if (d->depths[i] != (p < 0 ? 0 : d->depths[p] + 1)) return RB_ERR_INVALID_ARG;
+      if (d->ids[i] < 0 || d->ids[i] >= c.vocab) return RB_ERR_INVALID_ARG;
+    }
+    if (e->staged_pending) {
+      if (cudaEventSynchronize(e->staged) != cudaSuccess) return RB_ERR_CUDA;
+      e->staged_pending = false;
+    }
+    uint8_t* p = e->pinned;
+    memcpy(p, &sp, sizeof(sp));
+    memcpy(p + sizeof(sp), d->ids, n4);
+    memcpy(p + sizeof(sp) + n4, d->parents, n4);
+    memcpy(p + sizeof(sp) + 2 * n4, d->depths, n4);
+    // params, ids, parents, depths are laid out back to back in the workspace
+    // only up to alignment, so copy each piece to its place.
+    if (cudaMemcpyAsync(e->d_params, p, sizeof(sp), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(e->d_ids, p + sizeof(sp), n4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(e->d_parents, p + sizeof(sp) + n4, n4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(e->d_depths, p + sizeof(sp) + 2 * n4, n4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaEventRecord(e->staged, st) != cudaSuccess)
+      return RB_ERR_CUDA;
+    e->staged_pending = true;
+  } else {
+    if (e->staged_pending) {
+      if (cudaEventSynchronize(e->staged) != cudaSuccess) return RB_ERR_CUDA;
+      e->staged_pending = false;
+    }
+    memcpy(e->pinned, &sp, sizeof(sp));
+    if (cudaMemcpyAsync(e->d_params, e->pinned, sizeof(sp), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(e->d_ids, d->ids, n4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(e->d_parents, d->parents, n4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(e->d_depths, d->depths, n4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+        cudaEventRecord(e->staged, st) != cudaSuccess)
+      return RB_ERR_CUDA;
+    e->staged_pending = true;
+  }
+  const int rows = std::min(bucket_of(d->q), c.max_rows);  // workspace holds max_rows rows
+  if (!d->use_graph) return enqueue_step(e, rows, st);
+  auto it = e->graphs.find(rows);
+  if (it == e->graphs.end()) {
+    cudaGraph_t g = nullptr;
+    if (cudaStreamBeginCapture(e->cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return RB_ERR_CUDA;
+    const int r = enqueue_step(e, rows, e->cap);
+    const cudaError_t ce = cudaStreamEndCapture(e->cap, &g);
+    if (r != RB_OK) {
+      if (g) cudaGraphDestroy(g);
+      return r;
+    }
+    if (ce != cudaSuccess) return RB_ERR_CUDA;
+    cudaGraphExec_t ge = nullptr;
+    if (cudaGraphInstantiate(&ge, g, 0) != cudaSuccess) {
+      cudaGraphDestroy(g);
+      return RB_ERR_CUDA;
+    }
+    e->graph_defs[rows] = g;
+    it = e->graphs.emplace(rows, ge).first;
+  }
+  return cudaGraphLaunch(it->second, st) == cudaSuccess ? RB_OK : RB_ERR_CUDA;
+}
+
+int rb_engine_outputs(rb_engine* e, float** logits, int64_t** next_ids, void** hidden, void** kv_unused) {
+  (void)kv_unused;
+  if (!e) return RB_ERR_INVALID_ARG;
+  if (logits) *logits = e->logits;
+  if (next_ids) *next_ids = e->d_out;
+  if (hidden) *hidden = e->h;
+  return RB_OK;
+}
+
+int rb_engine_fetch_ids(rb_engine* e, int64_t* host, int n, void* stream) {
+  if (!e || !host || n < 0 || n > e->cfg.max_rows) return RB_ERR_INVALID_ARG;
+  if (n == 0) return RB_OK;
+  return cudaMemcpyAsync(host, e->d_out, static_cast<size_t>(n) * 8, cudaMemcpyDeviceToHost,
+                         static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? RB_OK
+             : RB_ERR_CUDA;
+}
+
+int rb_engine_compact(rb_engine* e, const int32_t* path, int n, int prompt_len, int base, void* stream) {
+  if (!e || (n > 0 && !path) || n < 0 || prompt_len < 0 || base < 0) return RB_ERR_INVALID_ARG;
+  if (n == 0) return RB_OK;
+  if (n > RB_COMPACT_MAX_SLOTS) return RB_ERR_CAPACITY;
+  std::vector<int32_t> src(n);
+  for (int i = 0; i < n; ++i) {
+    src[i] = prompt_len + base + path[i];
+    if (src[i] >= e->cfg.max_slots) return RB_ERR_CAPACITY;
+  }
+  const rb_model_config& c = e->cfg;
+  return compact_launch(e->kc.data(), e->vc.data(), c.n_layers, c.n_kv_heads, c.head_dim,
+                        static_cast<int64_t>(c.max_slots) * c.head_dim, c.head_dim, 2, src.data(), n,
+                        prompt_len + base, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

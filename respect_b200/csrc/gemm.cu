@@ -1,0 +1,359 @@
+// Row-count-invariant weight-streaming GEMM (tcgen05 + TMA, sm_100a).
+// Follows the contract of respect/kernels/gemm.py:11-41: fixed K order, fp32
+// accumulation, bf16 or fp32 output, bias handled by the caller.
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "gemm.cuh"
+#include "host_util.h"
+
+namespace rb {
+
+constexpr int kBK = 64;                          // K elements per stage: one 128-byte swizzle row
+constexpr int kTileM = 128;                      // token rows per MMA (M side)
+constexpr int kXTileBytes = kTileM * kBK * 2;    // 16 KB
+constexpr int kSmemLimit = 232448;               // 227 KB dynamic shared memory per CTA
+
+__host__ __device__ constexpr int pow2_cols(int c) {
+  return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512;
+}
+
+template <int BN, int MT>
+struct GemmCfg {
+  static constexpr int kWTileBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = MT * kXTileBytes + kWTileBytes;
+  static constexpr int kStagesRaw = (kSmemLimit - 1024 - 256) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
+  static constexpr int kAccStride = pow2_cols(BN);  // TMEM columns between token-tile accumulators
+  static constexpr int kTmemCols = MT * kAccStride;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 is 16..256 step 16");
+  static_assert(MT * pow2_cols(BN) <= 512, "TMEM holds 512 fp32 columns");
+  static_assert(kStages >= 2, "pipeline needs two stages");
+};
+
+struct GemmKernelArgs {
+  int M, N, K;
+  int k_chunks, splits;
+  void* out;
+  int64_t ldo;
+  float* partial;
+};
+
+template <int EPI>
+__device__ __forceinline__ void epi_store16(const GemmKernelArgs& a, int m, int n0, int split,
+                                            const float (&v)[16]) {
+  if (EPI == kEpiStoreBF16) {
+    uint16_t* o = static_cast<uint16_t*>(a.out) + static_cast<int64_t>(m) * a.ldo + n0;
+    if (n0 + 16 <= a.N && (a.ldo & 7) == 0) {
+      uint4 p0, p1;
+      p0.x = pack_bf16x2(v[0], v[1]);   p0.y = pack_bf16x2(v[2], v[3]);
+      p0.z = pack_bf16x2(v[4], v[5]);   p0.w = pack_bf16x2(v[6], v[7]);
+      p1.x = pack_bf16x2(v[8], v[9]);   p1.y = pack_bf16x2(v[10], v[11]);
+      p1.z = pack_bf16x2(v[12], v[13]); p1.w = pack_bf16x2(v[14], v[15]);
+      reinterpret_cast<uint4*>(o)[0] = p0;
+      reinterpret_cast<uint4*>(o)[1] = p1;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (n0 + i < a.N) o[i] = f32_to_bf16_bits(v[i]);
+    }
+  } else {
+    float* o;
+    int64_t ld;
+    if (EPI == kEpiStoreF32) {
+      o = static_cast<float*>(a.out) + static_cast<int64_t>(m) * a.ldo + n0;
+      ld = a.ldo;
+    } else {
+      o = a.partial + (static_cast<int64_t>(split) * a.M + m) * a.N + n0;
+      ld = a.N;
+    }
+    if (n0 + 16 <= a.N && (ld & 3) == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        reinterpret_cast<float4*>(o)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (n0 + i < a.N) o[i] = v[i];
+    }
+  }
+}
+
+// SiLU * mul with PyTorch eager rounding points: g, u are the bf16 GEMM
+// outputs; silu(g) = g / (1 + exp(-g)) in fp32 rounded to bf16, product rounded
+// to bf16 (respect/system/fused.py:106-113).
+__device__ __forceinline__ float silu_mul_bf16(float g_acc, float u_acc) {
+  const float g = round_bf16(g_acc);
+  const float u = round_bf16(u_acc);
+  const float s = round_bf16(g / (1.0f + expf(-g)));
+  return __fmul_rn(s, u);
+}
+
+template <int BN, int MT, int EPI>
+__global__ void __launch_bounds__(128, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
+                const GemmKernelArgs a) {
+  using C = GemmCfg<BN, MT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::kStages + 1);
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = smem_u32(bars + C::kStages);
+  const uint32_t accum = smem_u32(bars + 2 * C::kStages);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x, split = blockIdx.y, m_group = blockIdx.z;
+  const int kc0 = static_cast<int>(static_cast<int64_t>(split) * a.k_chunks / a.splits);
+  const int kc1 = static_cast<int>(static_cast<int64_t>(split + 1) * a.k_chunks / a.splits);
+  const int nk = kc1 - kc0;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmx);
+    tma_prefetch_desc(&tmw);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    mbar_init(accum, 1);
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // TMA producer: one stage = MT token tiles + one weight tile, 64 K-elements.
+    const uint64_t pol_w = policy_evict_first();
+    const uint64_t pol_x = policy_evict_last();
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % C::kStages;
+      const uint32_t ph = (i / C::kStages) & 1;
+      if (!mbar_wait(empty0 + 8 * s, ph ^ 1, 0x101)) break;
+      const uint32_t st = smem_u32(smem + s * C::kStageBytes);
+      mbar_arrive_expect_tx(full0 + 8 * s, C::kStageBytes);
+      const int kx = (kc0 + i) * kBK;
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+        tma_load_2d(st + mt * kXTileBytes, &tmx, full0 + 8 * s, kx, (m_group * MT + mt) * kTileM, pol_x);
+      tma_load_2d(st + MT * kXTileBytes, &tmw, full0 + 8 * s, kx, n_tile * BN, pol_w);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer: 4 K-steps of 16 per stage, one MMA per token tile per step.
+    constexpr uint32_t idesc = idesc_bf16_f32(kTileM, BN);
+    bool ok = true;
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % C::kStages;
+      const uint32_t ph = (i / C::kStages) & 1;
+      if (!mbar_wait(full0 + 8 * s, ph, 0x102)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t st = smem_u32(smem + s * C::kStageBytes);
+#pragma unroll
+      for (int kk = 0; kk < kBK / 16; ++kk) {
+        const uint64_t bdesc = sdesc_kmajor_sw128(st + MT * kXTileBytes + kk * 32);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          const uint64_t adesc = sdesc_kmajor_sw128(st + mt * kXTileBytes + kk * 32);
+          umma_bf16(tmem + mt * C::kAccStride, adesc, bdesc, idesc, (i | kk) != 0 ? 1u : 0u);
+        }
+      }
+      umma_commit(empty0 + 8 * s);
+    }
+    if (ok) umma_commit(accum);
+  }
+  __syncwarp();
+
+  // Epilogue: warp w owns TMEM lanes [32w, 32w+32) = token rows of each tile.
+  // tcgen05.ld is warp-collective: the whole warp takes the same branch.
+  const bool ok = __all_sync(0xffffffffu, mbar_wait(accum, 0, 0x103));
+  tc_fence_after();
+  if (ok) {
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+#pragma unroll 1
+    for (int mt = 0; mt < MT; ++mt) {
+      const int m = (m_group * MT + mt) * kTileM + warp * 32 + lane;
+      if (EPI == kEpiSiluMul) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float g[16], u[16];
+          tmem_ld16(lane_base + mt * C::kAccStride + c * 16, g);
+          tmem_ld16(lane_base + mt * C::kAccStride + BN / 2 + c * 16, u);
+          if (m < a.M) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) g[i] = silu_mul_bf16(g[i], u[i]);
+            // Output width is N / 2; BN/2 output columns per weight tile.
+            GemmKernelArgs b = a;
+            b.N = a.N / 2;
+            epi_store16<kEpiStoreBF16>(b, m, n_tile * (BN / 2) + c * 16, split, g);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 16; ++c) {
+          float v[16];
+          tmem_ld16(lane_base + mt * C::kAccStride + c * 16, v);
+          const int n0 = n_tile * BN + c * 16;
+          if (m < a.M && n0 < a.N) epi_store16<EPI>(a, m, n0, split, v);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// --------------------------------------------------------------------- host
+GemmShape gemm_plan(int M, int N, int K, int num_sms, int force_bn, int force_splits) {
+  GemmShape s{};
+  s.M = M; s.N = N; s.K = K;
+  s.k_chunks = (K + kBK - 1) / kBK;
+  int bn = 256;
+  if (force_bn) {
+    bn = force_bn;
+  } else {
+    const int n256 = (N + 255) / 256;
+    if (n256 > num_sms) {
+      // Many weight tiles: pick the width whose last wave is the fullest.
+      const int cands[3] = {256, 208, 128};
+      double best = -1.0;
+      for (int c : cands) {
+        const int t = (N + c - 1) / c;
+        const int waves = (t + num_sms - 1) / num_sms;
+        const double eff = static_cast<double>(t) / (static_cast<double>(waves) * num_sms);
+        if (eff > best + 0.02) { best = eff; bn = c; }
+      }
+    }
+  }
+  s.BN = bn;
+  s.n_tiles = (N + bn - 1) / bn;
+  int splits = 1;
+  if (force_splits) {
+    splits = force_splits;
+  } else if (s.n_tiles < num_sms) {
+    splits = std::max(1, std::min(num_sms / s.n_tiles, s.k_chunks / 4));
+  }
+  s.splits = std::max(1, std::min(splits, s.k_chunks));
+  s.mt = M > kTileM ? 2 : 1;
+  s.m_groups = (M + kTileM * s.mt - 1) / (kTileM * s.mt);
+  return s;
+}
+
+int gemm_encode_x(CUtensorMap* m, const void* x, int M, int K, int64_t ldx) {
+  return encode_2d_bf16(m, x, K, M, ldx, kBK, kTileM);
+}
+int gemm_encode_w(CUtensorMap* m, const void* w, int N, int K, int64_t ldw, int BN) {
+  return encode_2d_bf16(m, w, K, N, ldw, kBK, BN);
+}
+
+template <int BN, int MT, int EPI>
+static int launch_t(const GemmShape& s, const CUtensorMap& mx, const CUtensorMap& mw,
+                    const GemmKernelArgs& ka, cudaStream_t stream) {
+  using C = GemmCfg<BN, MT>;
+  auto kern = gemm_kernel<BN, MT, EPI>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
+    return RB_ERR_CUDA;
+  dim3 grid(s.n_tiles, s.splits, s.m_groups);
+  kern<<<grid, 128, C::kSmemBytes, stream>>>(mx, mw, ka);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;
+}
+
+template <int BN, int MT>
+static int launch_epi(const GemmShape& s, const CUtensorMap& mx, const CUtensorMap& mw,
+                      const GemmKernelArgs& ka, int epi, cudaStream_t stream) {
+  switch (epi) {
+    case kEpiStoreBF16: return launch_t<BN, MT, kEpiStoreBF16>(s, mx, mw, ka, stream);
+    case kEpiStoreF32: return launch_t<BN, MT, kEpiStoreF32>(s, mx, mw, ka, stream);
+    case kEpiSiluMul: return launch_t<BN, MT, kEpiSiluMul>(s, mx, mw, ka, stream);
+    case kEpiPartial: return launch_t<BN, MT, kEpiPartial>(s, mx, mw, ka, stream);
+  }
+  return RB_ERR_INVALID_ARG;
+}
+
+int gemm_launch_maps(const GemmShape& s, const CUtensorMap& mx, const CUtensorMap& mw,
+                     const GemmLaunch& a, cudaStream_t stream) {
+  GemmKernelArgs ka{};
+  ka.M = s.M; ka.N = s.N; ka.K = s.K;
+  ka.k_chunks = s.k_chunks;
+  ka.splits = s.splits;
+  ka.out = a.out;
+  ka.ldo = a.ldo;
+  ka.partial = a.partial;
+  if (a.epi == kEpiPartial ? a.partial == nullptr : a.out == nullptr) return RB_ERR_INVALID_ARG;
+  if (a.epi != kEpiPartial && s.splits != 1) return RB_ERR_INVALID_ARG;
+  if (a.epi == kEpiSiluMul && (s.N % s.BN) != 0) return RB_ERR_UNSUPPORTED;
+  const int key = s.BN * 4 + s.mt;
+  switch (key) {
+    case 256 * 4 + 1: return launch_epi<256, 1>(s, mx, mw, ka, a.epi, stream);
+    case 256 * 4 + 2: return launch_epi<256, 2>(s, mx, mw, ka, a.epi, stream);
+    case 208 * 4 + 1: return launch_epi<208, 1>(s, mx, mw, ka, a.epi, stream);
+    case 208 * 4 + 2: return launch_epi<208, 2>(s, mx, mw, ka, a.epi, stream);
+    case 128 * 4 + 1: return launch_epi<128, 1>(s, mx, mw, ka, a.epi, stream);
+    case 128 * 4 + 2: return launch_epi<128, 2>(s, mx, mw, ka, a.epi, stream);
+  }
+  return RB_ERR_UNSUPPORTED;
+}
+
+int gemm_launch(const GemmShape& s, const GemmLaunch& a, cudaStream_t stream) {
+  CUtensorMap mx, mw;
+  int st = gemm_encode_x(&mx, a.x, s.M, s.K, a.ldx);
+  if (st != RB_OK) return st;
+  st = gemm_encode_w(&mw, a.w, s.N, s.K, a.ldw, s.BN);
+  if (st != RB_OK) return st;
+  return gemm_launch_maps(s, mx, mw, a, stream);
+}
+
+// ------------------------------------------------------------ split-K reduce
+template <int OUT_F32>
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N,
+                                     void* __restrict__ out, int64_t ldo) {
+  const int m = blockIdx.y;
+  const int n = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (n >= N) return;
+  const int64_t plane = static_cast<int64_t>(M) * N;
+  const float* p = partial + static_cast<int64_t>(m) * N + n;
+  if (n + 4 <= N && (N & 3) == 0) {
+    float4 acc = *reinterpret_cast<const float4*>(p);
+    for (int s = 1; s < splits; ++s) {
+      const float4 t = *reinterpret_cast<const float4*>(p + s * plane);
+      acc.x += t.x; acc.y += t.y; acc.z += t.z; acc.w += t.w;
+    }
+    if (OUT_F32) {
+      float* o = static_cast<float*>(out) + static_cast<int64_t>(m) * ldo + n;
+      o[0] = acc.x; o[1] = acc.y; o[2] = acc.z; o[3] = acc.w;
+    } else {
+      uint16_t* o = static_cast<uint16_t*>(out) + static_cast<int64_t>(m) * ldo + n;
+      o[0] = f32_to_bf16_bits(acc.x); o[1] = f32_to_bf16_bits(acc.y);
+      o[2] = f32_to_bf16_bits(acc.z); o[3] = f32_to_bf16_bits(acc.w);
+    }
+  } else {
+    for (int j = n; j < n + 4 && j < N; ++j) {
+      float acc = p[j - n];
+      for (int s = 1; s < splits; ++s) acc += p[j - n + s * plane];
+      if (OUT_F32) static_cast<float*>(out)[static_cast<int64_t>(m) * ldo + j] = acc;
+      else static_cast<uint16_t*>(out)[static_cast<int64_t>(m) * ldo + j] = f32_to_bf16_bits(acc);
+    }
+  }
+}
+
+int splitk_reduce(const float* partial, int splits, int M, int N, void* out, int64_t ldo,
+                  int out_f32, cudaStream_t stream) {
+  if (M <= 0 || N <= 0) return RB_OK;
+  dim3 block(256);
+  dim3 grid((N + 4 * 256 - 1) / (4 * 256), M);
+  if (out_f32) splitk_reduce_kernel<1><<<grid, block, 0, stream>>>(partial, splits, M, N, out, ldo);
+  else splitk_reduce_kernel<0><<<grid, block, 0, stream>>>(partial, splits, M, N, out, ldo);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;
+}
+
+}  // namespace rb

@@ -1,0 +1,32 @@
+"""Linear layer whose result does not depend on the number of rows.
+
+Drop-in for ``respect.kernels.gemm.linear`` (respect/kernels/gemm.py:30-41).
+The tile keyword arguments are accepted and ignored: the native kernel
+(rb_linear, tcgen05 + TMA) fixes its own tile and K split from (N, K) alone,
+so a row gives the same bits alone or with other rows.
+"""
+from __future__ import annotations
+
+import torch
+
+from respect_b200 import _lib
+
+
+def linear(x, w, BM=32, BN=128, BK=64, num_warps=4, num_stages=2, out_dtype=None):
+    """x (..., K) @ w (N, K)^T -> (..., N). Bias is handled by the caller."""
+    K = x.shape[-1]
+    xs = x.reshape(-1, K).contiguous()
+    M = xs.shape[0]
+    N = w.shape[0]
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise TypeError("respect_b200.linear takes bf16 x and w")
+    if w.stride(-1) != 1:
+        w = w.contiguous()
+    od = out_dtype or x.dtype
+    out = torch.empty((M, N), device=x.device, dtype=od)
+    nbytes = _lib.lib().rb_linear_workspace(M, N, K)
+    ws = _lib.workspace(xs, nbytes)
+    _lib.call("rb_linear", xs.data_ptr(), xs.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(),
+              out.stride(0), _lib.dtype_code(od), M, N, K,
+              ws.data_ptr() if ws is not None else None, nbytes, _lib.stream_of(xs))
+    return out.reshape(*x.shape[:-1], N)

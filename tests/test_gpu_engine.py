@@ -1,0 +1,228 @@
+"""The native verify engine: parity with the numpy oracle (the reference's
+algorithm), bitwise equality with the composition of the standalone operators,
+and RESPECT's guarantee — committed tokens, logits and KV of a trie verify are
+bitwise equal to 1-token AR decoding with the same kernels (BASELINE configs 3/4)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import model as omodel
+from oracle.inputs import chain_seqs, top_up
+from respect_b200.candidates.trie import build_trie
+from respect_b200.decoding.acceptance import walk
+from respect_b200.decoding.engine import DecoderConfig, DecoderWeights, VerifyEngine
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def ar_decode(eng, first, n, prompt_len, act=(0, 0)):
+    """Greedy 1-token steps from `first`: returns tokens, per-step logits rows, next ids."""
+    toks, rows = [first], []
+    for t in range(n):
+        eng.step(np.array([toks[-1]], np.int32), np.array([-1], np.int32), np.array([0], np.int32), t, prompt_len,
+                 act_off=act[0], act_size=act[1])
+        rows.append(eng.logits(1)[0].clone())
+        toks.append(int(eng.fetch_ids(1)[0]))
+    return toks, rows
+
+
+def kv_slots(eng, lo, hi):
+    return [(k[:, lo:hi].clone(), v[:, lo:hi].clone()) for k, v in zip(eng.kc, eng.vc)]
+
+
+def trie_with_path(rng, path_tokens, n_nodes, vocab, n_chains=4):
+    """Candidates: the AR path plus seeded chains sharing a prefix with it (kept
+    while the merged trie stays within n_nodes), topped up to n_nodes."""
+    L = len(path_tokens)
+    seqs = [tuple(path_tokens)]
+    for _ in range(n_chains - 1):
+        share = int(rng.integers(1, L))
+        cand = tuple(path_tokens[:share]) + tuple(int(t) for t in rng.integers(0, vocab, L - share))
+        if len(build_trie(seqs + [cand]).nodes) <= n_nodes:
+            seqs.append(cand)
+    seqs = top_up(rng, seqs, n_nodes, vocab)
+    return build_trie(seqs)
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    cfg = DecoderConfig.tiny(2)
+    w = DecoderWeights.random(cfg, DEV, seed=1, std=0.05)
+    eng = VerifyEngine(w, max_rows=128, max_slots=1024)
+    yield cfg, w, eng
+    eng.close()
+
+
+def test_tiny_engine_matches_oracle(tiny):
+    cfg, w, eng = tiny
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, cfg.vocab, 200)
+    eng.prefill(prompt, chunk=64)
+    tree = build_trie(top_up(rng, chain_seqs(rng, 4, 12, cfg.vocab), 40, cfg.vocab))
+    eng.step(tree.tokens().astype(np.int32), tree.parents(), tree.depths(), 0, 200)
+    got = eng.logits(len(tree.nodes)).cpu().numpy()
+    W = omodel.weights_from_engine(w, cfg)
+    kc = [np.zeros((cfg.n_kv_heads, 1024, 128), np.float32) for _ in range(cfg.n_layers)]
+    vc = [np.zeros_like(k) for k in kc]
+    omodel.prefill(W, omodel.cfg_dict(cfg), prompt, kc, vc, chunk=64)
+    ref = omodel.verify_step(W, omodel.cfg_dict(cfg), tree.tokens(), tree.parents(), tree.depths(), 200, 0, kc, vc)
+    assert np.abs(got - ref).max() < 2e-2
+    ids = eng.next_ids(len(tree.nodes)).cpu().numpy()
+    ref_ids = ref.argmax(-1)
+    srt = np.sort(ref, axis=-1)
+    margin = srt[:, -1] - srt[:, -2]
+    # committed-token parity: any disagreement must be a near-tie below the logit tolerance
+    assert np.all((ids == ref_ids) | (margin < 2e-2))
+    # prompt KV written by the engine's prefill matches the oracle's
+    for l in range(cfg.n_layers):
+        assert np.abs(eng.kc[l][:, :200].float().cpu().numpy() - kc[l][:, :200]).max() < 2e-2
+
+
+def test_tiny_trie_vs_ar_bitwise(tiny):
+    cfg, w, eng = tiny
+    rng = np.random.default_rng(1)
+    P = 300
+    eng.prefill(rng.integers(0, cfg.vocab, P), chunk=128)
+    first = int(rng.integers(0, cfg.vocab))
+    toks, ar_rows = ar_decode(eng, first, 20, P)
+    ar_kv = kv_slots(eng, P, P + 20)
+    tree = trie_with_path(rng, toks[:20], 100, cfg.vocab)
+    am = eng.verify(tree, P, 0)
+    path, acc, rec = walk(tree, first, 128, -1, lambda a, ch: int(am[ch]))
+    assert acc == toks[:len(acc)] and len(acc) == 20 and rec == toks[20]
+    lg = eng.logits(len(tree.nodes))
+    for t, node in enumerate(path):
+        assert torch.equal(lg[node], ar_rows[t])
+    eng.compact(path, P, 0)
+    for (ka, va), (kb, vb) in zip(ar_kv, kv_slots(eng, P, P + 20)):
+        assert torch.equal(ka, kb) and torch.equal(va, vb)
+
+
+def _compose_layer0(w, eng, cfg, tree, P, base):
+    """One layer + head through the standalone operators (torch only moves data)."""
+    from respect_b200.kernels.attention import fused_attn_hyb
+    from respect_b200.kernels.gemm import linear
+    from respect_b200.kernels.rmsnorm import rmsnorm
+    from respect_b200.system.fused import rope, silu_mul
+    H, HK, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    lw = w.layers[0]
+    q = len(tree.nodes)
+    ids = torch.from_numpy(tree.tokens()).to(DEV)
+    h = w.embed[ids]
+    x = rmsnorm(h, lw["in_norm"], cfg.rms_eps)
+    qkv = linear(x, lw["wqkv"])
+    qh = rmsnorm(qkv[:, :H * D].reshape(q, H, D), lw["q_norm"], cfg.rms_eps)
+    kh = rmsnorm(qkv[:, H * D:(H + HK) * D].reshape(q, HK, D), lw["k_norm"], cfg.rms_eps)
+    vh = qkv[:, (H + HK) * D:].reshape(q, HK, D)
+    pos = torch.from_numpy(P + base + tree.depths()).to(DEV).long()
+    cos, sin = eng.cos[pos][None], eng.sin[pos][None]
+    qh = rope(qh.transpose(0, 1)[None], cos, sin)[0]          # [H, q, D]
+    kh = rope(kh.transpose(0, 1)[None], cos, sin)[0]          # [HK, q, D]
+    kc, vc = eng.kc[0].clone(), eng.vc[0].clone()
+    kc[:, P + base:P + base + q] = kh
+    vc[:, P + base:P + base + q] = vh.transpose(0, 1)
+    n_node = base + q
+    NN = ((n_node + 31) // 32) * 32
+    msk = torch.zeros(q, NN, dtype=torch.bool, device=DEV)
+    msk[:, :base] = True
+    msk[:, base:n_node] = torch.from_numpy(np.asarray(__import__("respect_b200.candidates.trie",
+                                                                   fromlist=["x"]).trie_ancestry(tree))).to(DEV)
+    kn = torch.zeros(HK, NN, D, dtype=torch.bfloat16, device=DEV)
+    vn = torch.zeros_like(kn)
+    kn[:, :n_node] = kc[:, P:P + n_node]
+    vn[:, :n_node] = vc[:, P:P + n_node]
+    a = fused_attn_hyb(qh.contiguous(), kc[:, :P], vc[:, :P], kn, vn, msk)
+    a = a.transpose(0, 1).reshape(q, H * D)
+    h = h + linear(a, lw["wo"])
+    x = rmsnorm(h, lw["post_norm"], cfg.rms_eps)
+    gu = linear(x, lw["wgu"]).view(q, cfg.ffn // 128, 2, 128)
+    act = silu_mul(gu[:, :, 0].reshape(q, cfg.ffn).contiguous(), gu[:, :, 1].reshape(q, cfg.ffn).contiguous())
+    h = h + linear(act, lw["wd"])
+    x = rmsnorm(h, w.final_norm, cfg.rms_eps)
+    return linear(x, w.lm_head, out_dtype=torch.float32), kc, vc
+
+
+def test_engine_equals_operator_composition_7b_layer():
+    """Config-3 dimensions, one layer: the fused engine step is bitwise equal to
+    the standalone operators composed (rb_linear, rb_rmsnorm, rb_rope,
+    rb_fused_attn_hyb, rb_silu_mul), including the KV it writes."""
+    cfg = DecoderConfig(3584, 1, 28, 4, 128, 18944, 152064)
+    w = DecoderWeights.random(cfg, DEV, seed=2)
+    eng = VerifyEngine(w, max_rows=128, max_slots=2048)
+    try:
+        rng = np.random.default_rng(2)
+        P = 700
+        eng.prefill(rng.integers(0, cfg.vocab, P))
+        base = 3
+        eng.step(rng.integers(0, cfg.vocab, base).astype(np.int32), np.array([-1, 0, 1], np.int32),
+                 np.arange(3, dtype=np.int32), 0, P)
+        tree = build_trie(top_up(rng, chain_seqs(rng, 4, 16, cfg.vocab), 64, cfg.vocab))
+        ref_logits, kc, vc = _compose_layer0(w, eng, cfg, tree, P, base)
+        eng.step(tree.tokens().astype(np.int32), tree.parents(), tree.depths(), base, P)
+        assert torch.equal(eng.logits(len(tree.nodes)), ref_logits)
+        assert torch.equal(eng.kc[0], kc) and torch.equal(eng.vc[0], vc)
+    finally:
+        eng.close()
+
+
+@pytest.fixture(scope="module")
+def big():
+    cfg = DecoderConfig.baseline_7b()
+    w = DecoderWeights.random(cfg, DEV, seed=0)
+    eng = VerifyEngine(w, max_rows=512, max_slots=4096)
+    yield cfg, w, eng
+    eng.close()
+
+
+def test_7b_trie_vs_ar_bitwise(big):
+    """Config 3: prefix 3000, 128-node trie of 4 chains of 32 with the model's own
+    AR output as one chain; committed tokens, their logits and KV equal AR bitwise."""
+    cfg, w, eng = big
+    rng = np.random.default_rng(3)
+    P = 3000
+    eng.prefill(rng.integers(0, cfg.vocab, P))
+    first = int(rng.integers(0, cfg.vocab))
+    toks, ar_rows = ar_decode(eng, first, 32, P)
+    ar_kv = kv_slots(eng, P, P + 32)
+    tree = trie_with_path(rng, toks[:32], 128, cfg.vocab)
+    assert len(tree.nodes) == 128
+    am = eng.verify(tree, P, 0)
+    path, acc, rec = walk(tree, first, 128, -1, lambda a, ch: int(am[ch]))
+    assert acc == toks[:32] and rec == toks[32]
+    lg = eng.logits(128)
+    for t, node in enumerate(path):
+        assert torch.equal(lg[node], ar_rows[t])
+    eng.compact(path, P, 0)
+    for (ka, va), (kb, vb) in zip(ar_kv, kv_slots(eng, P, P + 32)):
+        assert torch.equal(ka, kb) and torch.equal(va, vb)
+
+
+@pytest.mark.parametrize("P", [2999, 3071, 3072, 3073, 3129])
+def test_7b_invariance_sweep(big, P):
+    """Config 4: the same 32-token path inside tries of 32/64/256/512 nodes gives
+    bitwise identical committed-node logits, at prefix lengths around tile
+    boundaries."""
+    cfg, w, eng = big
+    rng = np.random.default_rng(P)
+    eng.prefill(rng.integers(0, cfg.vocab, P))
+    path_toks = [int(t) for t in rng.integers(0, cfg.vocab, 32)]
+    ref = None
+    for n in (32, 64, 256, 512):
+        tree = trie_with_path(np.random.default_rng(n), path_toks, n, cfg.vocab)
+        assert len(tree.nodes) == n
+        eng.step(tree.tokens().astype(np.int32), tree.parents(), tree.depths(), 0, P)
+        # node index of the path's d-th token: follow the trie from the root
+        idx, node = [], tree.roots[path_toks[0]]
+        for d in range(32):
+            idx.append(node)
+            if d + 1 < 32:
+                node = tree.nodes[node].children[path_toks[d + 1]]
+        rows = eng.logits(n)[idx].clone()
+        kv = [(k[:, P + torch.tensor(idx, device=DEV)].clone()) for k in eng.kc[:2]]
+        if ref is None:
+            ref = (rows, kv)
+        else:
+            assert torch.equal(rows, ref[0])
+            for a, b in zip(kv, ref[1]):
+                assert torch.equal(a, b)

@@ -1,0 +1,91 @@
+"""Host-side logic of respect_b200 (no GPU): the trie / acceptance mirror against
+the reference's golden vectors, and the C ABI surface of the native library."""
+import ctypes
+import json
+import re
+from pathlib import Path
+
+import numpy as np
+
+from respect_b200.candidates.trie import build_trie, trie_ancestry
+from respect_b200.decoding.acceptance import walk
+
+ROOT = Path(__file__).resolve().parents[1]
+G = ROOT / "tests" / "golden"
+
+
+def test_trie_and_walk_match_reference_golden():
+    for c in json.loads((G / "trie.json").read_text()):
+        t = build_trie([tuple(s) for s in c["seqs"]])
+        nodes = [[n.token, -1 if n.parent is None else n.parent, n.depth] for n in t.nodes]
+        assert nodes == c["nodes"], c["name"]
+        assert [[k, v] for k, v in t.roots.items()] == c["roots"]
+        assert [list(s) for s in t.seqs] == c["unique"]
+        anc = trie_ancestry(t)
+        assert [np.flatnonzero(anc[i]).tolist() for i in range(len(t.nodes))] == c["ancestry"]
+        assert np.array_equal(t.parents(), np.array([n[1] for n in nodes], np.int32))
+        assert np.array_equal(t.depths(), np.array([n[2] for n in nodes], np.int32))
+        for w in c["walks"]:
+            tg = {int(k): v for k, v in w["target"].items()}
+            path, acc, rec = walk(t, w["first"], w["cap"], w["eos"], lambda a, ch: tg[ch])
+            assert (path, acc, rec) == (w["path"], w["acc"], w["rec"])
+
+
+def test_reference_trie_unit_cases():
+    eos = 99
+    t = build_trie([(1, 2, 3, eos), (1, 2, 4, eos), (1, 2, 3, eos)])
+    assert [n.token for n in t.nodes] == [1, 2, 3, eos, 4, eos] and len(t.seqs) == 2
+    t = build_trie([(1, 2, 3), (1, 5)])
+    assert all(n.parent is None or n.parent < i for i, n in enumerate(t.nodes))
+    assert np.flatnonzero(trie_ancestry(t)[3]).tolist() == [0, 3]
+    t = build_trie([(1, 2, 3, eos)])
+    target = {0: 2, 1: 9}
+    assert walk(t, 1, 128, eos, lambda a, ch: target[ch]) == ([0, 1], [1, 2], 9)
+    t = build_trie([(1, eos)])
+    assert walk(t, 1, 128, eos, lambda a, ch: eos)[1] == [1, eos]
+    # empty trie / unknown first token: nothing accepted, correction = first
+    assert walk(build_trie([]), 5, 10, eos, lambda a, ch: 0) == ([], [], 5)
+
+
+def _declared_symbols():
+    text = (ROOT / "include" / "respect_b200.h").read_text()
+    return sorted(set(re.findall(r"RB_API\s+[\w\s\*]+?\b(rb_\w+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    from respect_b200 import _lib
+    lib = _lib.lib()
+    names = _declared_symbols()
+    assert len(names) >= 20
+    for n in names:
+        assert hasattr(lib, n), n
+    assert lib.rb_abi_version() == 1
+    assert lib.rb_status_string(2) == b"unsupported shape, dtype or layout"
+
+
+def test_capi_rejects_bad_arguments_without_a_gpu():
+    """Host-side validation runs before any CUDA call: bad arguments return an
+    error code (never reach a kernel)."""
+    from respect_b200 import _lib
+    lib = _lib.lib()
+    assert lib.rb_linear(None, 8, None, 8, None, 8, _lib.RB_BF16, 1, 8, 8, None, 0, None) == 1
+    assert lib.rb_silu_mul(None, None, None, 10, _lib.RB_BF16, None) == 1
+    assert lib.rb_trie_node_mask(None, 4, 0, 2, 4, None, 4, None) == 1      # M < q
+    args = _lib.AttnArgs()
+    args.dtype, args.H, args.HK, args.D, args.M = _lib.RB_BF16, 28, 4, 64, 1   # head_dim 64 unsupported
+    assert lib.rb_fused_attn_hyb(ctypes.byref(args), None, 0, None) in (1, 2)
+    assert lib.rb_engine_workspace_bytes(None) == 0
+
+
+def test_engine_config_validation():
+    from respect_b200.decoding import engine as E
+    lib = __import__("respect_b200._lib", fromlist=["x"]).lib()
+    fn = lib.rb_engine_workspace_bytes
+    fn.restype, fn.argtypes = ctypes.c_size_t, [ctypes.POINTER(E._Cfg)]
+    good = E._Cfg(3584, 28, 28, 4, 128, 18944, 152064, 1e-6, 128, 4096, 8192)
+    assert fn(ctypes.byref(good)) > 0
+    bad = E._Cfg(3584, 28, 28, 4, 64, 18944, 152064, 1e-6, 128, 4096, 8192)   # head_dim 64
+    assert fn(ctypes.byref(bad)) == 0
+    cfg = E.DecoderConfig.baseline_7b()
+    # weights streamed per step: 6.525 G layer params + 0.545 G lm_head (bf16)
+    assert abs(cfg.weight_bytes_per_step() / 1e9 - 14.14) < 0.01
