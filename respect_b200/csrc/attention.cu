@@ -273,19 +273,24 @@ int attn_validate(const rb_attn_args* a) {
   if (a->H <= 0 || a->HK <= 0 || a->M < 0 || a->NP < 0 || a->NN < 0) return RB_ERR_INVALID_ARG;
   if (a->H % a->HK != 0) return RB_ERR_INVALID_ARG;
   if (a->D != 128) return RB_ERR_UNSUPPORTED;
-  if (a->sqd != 1 || a->skpd != 1 || a->svpd != 1 || a->sknd != 1 || a->svnd != 1 || a->sod != 1)
+  if (a->sqd != 1 || a->sod != 1 || (a->NP > 0 && (a->skpd != 1 || a->svpd != 1)) ||
+      (a->NN > 0 && (a->sknd != 1 || a->svnd != 1)))
     return RB_ERR_UNSUPPORTED;
   if (!a->q || !a->out || (a->NP > 0 && (!a->kp || !a->vp)) || (a->NN > 0 && (!a->kn || !a->vn)))
     return RB_ERR_INVALID_ARG;
   if (a->mask_kind < RB_MASK_BOOL || a->mask_kind > RB_MASK_CAUSAL) return RB_ERR_INVALID_ARG;
   if (a->mask_kind != RB_MASK_CAUSAL && a->NN > 0 && !a->msk) return RB_ERR_INVALID_ARG;
-  // Vector loads of 4 elements need 4-element-aligned row strides and bases.
-  const int64_t strides[] = {a->sqh, a->sqm, a->skph, a->skpn, a->svph, a->svpn,
-                             a->sknh, a->sknn, a->svnh, a->svnn, a->soh, a->som};
+  // Vector loads of 4 elements need 4-element-aligned row strides and bases
+  // (only for the tensors a call actually reads).
+  const bool pre = a->NP > 0, nod = a->NN > 0;
+  const int64_t strides[] = {a->sqh, a->sqm, a->soh, a->som,
+                             pre ? a->skph : 0, pre ? a->skpn : 0, pre ? a->svph : 0, pre ? a->svpn : 0,
+                             nod ? a->sknh : 0, nod ? a->sknn : 0, nod ? a->svnh : 0, nod ? a->svnn : 0};
   for (int64_t s : strides)
     if (s % 4 != 0) return RB_ERR_UNSUPPORTED;
   const int eb = a->dtype == RB_F32 ? 4 : 2;
-  const void* ptrs[] = {a->q, a->kp, a->vp, a->kn, a->vn, a->out};
+  const void* ptrs[] = {a->q, pre ? a->kp : nullptr, pre ? a->vp : nullptr, nod ? a->kn : nullptr,
+                        nod ? a->vn : nullptr, a->out};
   for (const void* ptr : ptrs)
     if (ptr && (reinterpret_cast<uintptr_t>(ptr) % (4 * eb)) != 0) return RB_ERR_UNSUPPORTED;
   return RB_OK;
@@ -311,10 +316,19 @@ int attn_launch(const rb_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t s
   float* part = static_cast<float*>(ws);
   const int nchunks = (a->NP + kPrefixChunk - 1) / kPrefixChunk;
   if (nchunks > 0) {
-    dim3 grid(nchunks, a->H, (a->M + 15) / 16);
-    if (a->dtype == RB_F32) attn_prefix_simt<float><<<grid, 128, 0, stream>>>(p, part, nchunks);
-    else attn_prefix_simt<uint16_t><<<grid, 128, 0, stream>>>(p, part, nchunks);
-    if (cudaGetLastError() != cudaSuccess) return RB_ERR_CUDA;
+    if (a->dtype == RB_F32) {  // fp32: CUDA-core FFMA (the 1e-5 parity bar rules out tf32 MMAs)
+      dim3 grid(nchunks, a->H, (a->M + 15) / 16);
+      attn_prefix_simt<float><<<grid, 128, 0, stream>>>(p, part, nchunks);
+      if (cudaGetLastError() != cudaSuccess) return RB_ERR_CUDA;
+    } else {  // bf16: tcgen05 QK^T / PV with TMA-staged tiles
+      CUtensorMap tq, tk, tv;
+      if (encode_heads_3d(&tq, a->q, a->M, a->H, a->sqm, a->sqh) != RB_OK ||
+          encode_heads_3d(&tk, a->kp, a->NP, a->HK, a->skpn, a->skph) != RB_OK ||
+          encode_heads_3d(&tv, a->vp, a->NP, a->HK, a->svpn, a->svph) != RB_OK)
+        return RB_ERR_UNSUPPORTED;  // TMA needs 16-byte aligned bases and row strides
+      const int st = attn_prefix_tc_launch(tq, tk, tv, p, part, nchunks, stream);
+      if (st != RB_OK) return st;
+    }
   }
   dim3 grid2((a->M + 3) / 4, a->H);
   if (a->dtype == RB_F32) attn_nodes<float><<<grid2, 128, 0, stream>>>(p, part);
@@ -323,10 +337,10 @@ int attn_launch(const rb_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t s
 }
 
 // Engine path: bf16, q/base/PL from device memory, trie masking from parents.
-int attn_launch_engine(const AttnDev& p, float* part, int max_chunks, cudaStream_t stream) {
-  dim3 grid(max_chunks, p.H, (p.M + 15) / 16);
-  attn_prefix_simt<uint16_t><<<grid, 128, 0, stream>>>(p, part, max_chunks);
-  if (cudaGetLastError() != cudaSuccess) return RB_ERR_CUDA;
+int attn_launch_engine(const AttnDev& p, float* part, int max_chunks, const CUtensorMap& tq,
+                       const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t stream) {
+  const int st = attn_prefix_tc_launch(tq, tk, tv, p, part, max_chunks, stream);
+  if (st != RB_OK) return st;
   dim3 grid2((p.M + 3) / 4, p.H);
   attn_nodes<uint16_t><<<grid2, 128, 0, stream>>>(p, part);
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;

@@ -1,6 +1,7 @@
 // Trie-verification attention: device parameter block and launchers.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -48,6 +49,11 @@ struct AttnDev {
 size_t attn_workspace_bytes(int H, int M, int D, int NP);
 int attn_validate(const rb_attn_args* a);
 int attn_launch(const rb_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t stream);
-int attn_launch_engine(const AttnDev& p, float* part, int max_chunks, cudaStream_t stream);
+int attn_launch_engine(const AttnDev& p, float* part, int max_chunks, const CUtensorMap& tq,
+                       const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t stream);
+// 3-D tensor map of [heads, rows, 128] bf16 with 64 x 128 x 1 boxes (TMA, 128-byte swizzle).
+int encode_heads_3d(CUtensorMap* m, const void* base, int rows, int heads, int64_t ld_row, int64_t ld_head);
+int attn_prefix_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const AttnDev& p,
+                          float* part, int nchunks, cudaStream_t stream);
 
 }  // namespace rb

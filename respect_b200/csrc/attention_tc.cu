@@ -1,0 +1,239 @@
+// Prefix phase of the trie attention on the 5th-generation tensor cores
+// (bf16 inputs, head_dim 128). One CTA = one query head x 128 query rows x one
+// fixed prefix chunk of kPrefixChunk keys at absolute positions; keys are
+// processed in tiles of 128 in ascending order (respect/kernels/attention.py:36-50):
+//
+//   S = Q K^T            tcgen05.mma, M=128 rows, N=128 keys, K=128 dims -> TMEM
+//   m' = max(m, rowmax(S*scale)); alpha = 2^(m - m'); p = 2^(S*scale - m')
+//   O = bf16(p) V        tcgen05.mma, A = P (smem, K-major), B = V (MN-major)
+//   acc = acc*alpha + O; l = l*alpha + sum(p)     (fp32, one row per thread)
+//
+// Warp roles: warps 0-3 softmax / correction (thread = query row = TMEM lane),
+// warp 4 TMA producer (Q once, K/V double-buffered), warp 5 MMA issuer and
+// TMEM owner. Each row's result depends only on that row and the chunk's keys:
+// the MMA computes rows independently and every row reduction runs in a
+// fixed order, so a row gives the same bits whatever the other rows are.
+#include "attention.cuh"
+#include "common.cuh"
+#include "host_util.h"
+
+namespace rb {
+
+namespace tc {
+constexpr int kRows = 128, kKeys = 128, kD = 128;
+constexpr int kHalf = 128 * 64 * 2;          // one 64-element-wide swizzled half tile: 16 KB
+constexpr int kQOff = 0;                     // Q: 2 halves
+constexpr int kKVOff = 2 * kHalf;            // 2 stages x (K 2 halves, V 2 halves)
+constexpr int kStage = 4 * kHalf;            // 64 KB
+constexpr int kPOff = kKVOff + 2 * kStage;   // P: 2 halves (keys 0-63 | 64-127)
+constexpr int kBarOff = kPOff + 2 * kHalf;   // 192 KB
+constexpr int kSmem = 1024 + kBarOff + 256;
+constexpr int kThreads = 192;
+// barrier indices
+enum { Q_FULL = 0, KV_FULL = 1, KV_EMPTY = 3, S_FULL = 5, P_FULL = 7, O_FULL = 8, O_FREE = 9, NBAR = 10 };
+constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, 0, 0);
+constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, 0, 1);
+}  // namespace tc
+
+__global__ void __launch_bounds__(tc::kThreads, 1)
+    attn_prefix_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                   const __grid_constant__ CUtensorMap tv, const AttnDev p, float* __restrict__ part) {
+  using namespace tc;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBAR);
+  auto bar = [&](int i) { return smem_u32(bars + i); };
+
+  const int c = blockIdx.x, h = blockIdx.y, rt = blockIdx.z;
+  const int NP = p.sp ? p.sp->prompt_len : p.NP;
+  const int M = p.sp ? min(p.M, p.sp->q) : p.M;
+  const int k0 = c * kPrefixChunk;
+  const int k1 = min(NP, k0 + kPrefixChunk);
+  if (k0 >= k1 || rt * kRows >= M) return;  // uniform per CTA, before any barrier exists
+  const int ntiles = (k1 - k0 + kKeys - 1) / kKeys;
+  const int kvh = h / (p.H / p.HK);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+    mbar_init(bar(Q_FULL), 1);
+    mbar_init(bar(KV_FULL), 1);
+    mbar_init(bar(KV_FULL + 1), 1);
+    mbar_init(bar(KV_EMPTY), 1);
+    mbar_init(bar(KV_EMPTY + 1), 1);
+    mbar_init(bar(S_FULL), 1);
+    mbar_init(bar(S_FULL + 1), 1);
+    mbar_init(bar(P_FULL), 128);
+    mbar_init(bar(O_FULL), 1);
+    mbar_init(bar(O_FREE), 128);
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sQ = smem_u32(smem + kQOff), sKV = smem_u32(smem + kKVOff), sP = smem_u32(smem + kPOff);
+
+  if (warp == 4) {
+    if (lane == 0) {  // TMA producer
+      const uint64_t pol = policy_evict_last();
+      mbar_arrive_expect_tx(bar(Q_FULL), 2 * kHalf);
+      tma_load_3d(sQ, &tq, bar(Q_FULL), 0, rt * kRows, h, pol);
+      tma_load_3d(sQ + kHalf, &tq, bar(Q_FULL), 64, rt * kRows, h, pol);
+      for (int j = 0; j < ntiles; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(bar(KV_EMPTY + s), ((j >> 1) & 1) ^ 1, 0x211)) break;
+        const uint32_t st = sKV + s * kStage;
+        const int key = k0 + j * kKeys;
+        mbar_arrive_expect_tx(bar(KV_FULL + s), kStage);
+        tma_load_3d(st, &tk, bar(KV_FULL + s), 0, key, kvh, pol);
+        tma_load_3d(st + kHalf, &tk, bar(KV_FULL + s), 64, key, kvh, pol);
+        tma_load_3d(st + 2 * kHalf, &tv, bar(KV_FULL + s), 0, key, kvh, pol);
+        tma_load_3d(st + 3 * kHalf, &tv, bar(KV_FULL + s), 64, key, kvh, pol);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {  // MMA issuer
+      auto issue_qk = [&](int j) {
+        const uint32_t st = sKV + (j & 1) * kStage;
+        const uint32_t d = tmem + (j & 1) * 128;
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+          umma_bf16(d, sdesc_kmajor_sw128(sQ + off), sdesc_kmajor_sw128(st + off), kIdescQK, kk ? 1u : 0u);
+        }
+        umma_commit(bar(S_FULL + (j & 1)));
+      };
+      bool ok = mbar_wait(bar(Q_FULL), 0, 0x212) && mbar_wait(bar(KV_FULL), 0, 0x213);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0);
+      }
+      for (int j = 0; ok && j < ntiles; ++j) {
+        if (j + 1 < ntiles) {
+          if (!mbar_wait(bar(KV_FULL + ((j + 1) & 1)), ((j + 1) >> 1) & 1, 0x214)) break;
+          tc_fence_after();
+          issue_qk(j + 1);
+        }
+        if (!mbar_wait(bar(P_FULL), j & 1, 0x215)) break;
+        if (j > 0 && !mbar_wait(bar(O_FREE), (j - 1) & 1, 0x216)) break;
+        tc_fence_after();
+        const uint32_t sv = sKV + (j & 1) * kStage + 2 * kHalf;
+#pragma unroll
+        for (int kk = 0; kk < kKeys / 16; ++kk) {
+          const uint32_t pa = sP + (kk >> 2) * kHalf + (kk & 3) * 32;
+          umma_bf16(tmem + 256, sdesc_kmajor_sw128(pa), sdesc_mnmajor_sw128(sv + kk * 2048, kHalf), kIdescPV,
+                    kk ? 1u : 0u);
+        }
+        umma_commit(bar(O_FULL));
+        if (j + 2 < ntiles) umma_commit(bar(KV_EMPTY + (j & 1)));
+      }
+    }
+  } else {
+    // Softmax / correction: thread = row (TMEM lane 32*warp + lane).
+    const int r = threadIdx.x;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const float scale2 = p.sm_scale * 1.4426950408889634f;
+    float m = -INFINITY, l = 0.f;
+    float acc[kD];
+#pragma unroll
+    for (int i = 0; i < kD; ++i) acc[i] = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(S_FULL + (j & 1)), (j >> 1) & 1, 0x217));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t sb = lane_base + (j & 1) * 128;
+      const int nvalid = min(kKeys, k1 - (k0 + j * kKeys));
+      float mx = -INFINITY;
+#pragma unroll
+      for (int cc = 0; cc < kKeys / 16; ++cc) {
+        float v[16];
+        tmem_ld16(sb + cc * 16, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) mx = fmaxf(mx, cc * 16 + i < nvalid ? v[i] * scale2 : -INFINITY);
+      }
+      const float m_new = fmaxf(m, mx);
+      const float alpha = fast_exp2(m - m_new);
+      float rs = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < kKeys / 16; ++cc) {
+        float v[16];
+        tmem_ld16(sb + cc * 16, v);
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const float p0 = cc * 16 + i < nvalid ? fast_exp2(v[i] * scale2 - m_new) : 0.f;
+          const float p1 = cc * 16 + i + 1 < nvalid ? fast_exp2(v[i + 1] * scale2 - m_new) : 0.f;
+          rs += p0;
+          rs += p1;
+          w[i / 2] = pack_bf16x2(p0, p1);
+        }
+        // keys cc*16 .. cc*16+15 = two 16-byte chunks of the 128-byte swizzled row
+        const int half = cc >> 2, ch = (cc & 3) * 2;
+        uint8_t* rowp = smem + kPOff + half * kHalf + r * 128;
+        *reinterpret_cast<uint4*>(rowp + (((ch) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(rowp + (((ch + 1) ^ (r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+      l = fmaf(l, alpha, rs);
+      fence_proxy_async_smem();  // P stores -> visible to the tensor core (async proxy)
+      tc_fence_before();         // S loads of this tile ordered before the arrive
+      mbar_arrive(bar(P_FULL));
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(O_FULL), j & 1, 0x218));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int cc = 0; cc < kD / 16; ++cc) {
+        float o[16];
+        tmem_ld16(lane_base + 256 + cc * 16, o);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[cc * 16 + i] = fmaf(acc[cc * 16 + i], alpha, o[i]);
+      }
+      tc_fence_before();
+      mbar_arrive(bar(O_FREE));
+      m = m_new;
+    }
+    const int row = rt * kRows + r;
+    if (ok && row < M) {
+      float* o = part + ((static_cast<int64_t>(c) * p.H + h) * p.M + row) * kPartStride;
+#pragma unroll
+      for (int i = 0; i < kD; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+      o[kD] = m;
+      o[kD + 1] = l;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// [H, rows, 128] bf16 (rows `ld_row` elements apart, heads `ld_head` apart) as a
+// 3-D tensor map with 64 x 128 x 1 boxes.
+int encode_heads_3d(CUtensorMap* m, const void* base, int rows, int heads, int64_t ld_row, int64_t ld_head) {
+  const uint64_t dims[3] = {128, static_cast<uint64_t>(rows), static_cast<uint64_t>(heads)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(ld_row) * 2, static_cast<uint64_t>(ld_head) * 2};
+  const uint32_t box[3] = {64, 128, 1};
+  return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int attn_prefix_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const AttnDev& p,
+                          float* part, int nchunks, cudaStream_t stream) {
+  static_assert(tc::kSmem <= 232448, "shared memory budget");
+  if (cudaFuncSetAttribute(attn_prefix_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmem) != cudaSuccess)
+    return RB_ERR_CUDA;
+  dim3 grid(nchunks, p.H, (p.M + tc::kRows - 1) / tc::kRows);
+  attn_prefix_tc<<<grid, tc::kThreads, tc::kSmem, stream>>>(tq, tk, tv, p, part);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;
+}
+
+}  // namespace rb

@@ -232,7 +232,7 @@ struct rb_engine {
   int max_chunks = 1;
   // tensor maps
   CUtensorMap m_xn, m_attn, m_act, m_lm;
-  std::vector<CUtensorMap> m_qkv, m_o, m_gu, m_d;
+  std::vector<CUtensorMap> m_qkv, m_o, m_gu, m_d, m_kc, m_vc;
   int bn_lm = 256;
   // host staging and graphs
   uint8_t* pinned = nullptr;
@@ -262,7 +262,9 @@ Layout layout_of(const rb_model_config& c) {
   const GemmShape s_qkv = gemm_plan(c.max_rows, nqkv, c.hidden, nsm);
   const GemmShape s_o = gemm_plan(c.max_rows, c.hidden, c.n_heads * c.head_dim, nsm);
   const GemmShape s_d = gemm_plan(c.max_rows, c.hidden, c.ffn, nsm);
+  const GemmShape s_lm = gemm_plan(c.max_rows, c.vocab, c.hidden, nsm);
   size_t part_elems = static_cast<size_t>(s_qkv.splits) * nqkv;
+  if (s_lm.splits > 1) part_elems = std::max(part_elems, static_cast<size_t>(s_lm.splits) * c.vocab);
   part_elems = std::max(part_elems, static_cast<size_t>(s_o.splits) * c.hidden);
   part_elems = std::max(part_elems, static_cast<size_t>(s_d.splits) * c.hidden);
   const int max_chunks = (c.max_slots + kPrefixChunk - 1) / kPrefixChunk;
@@ -363,7 +365,9 @@ int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
     p.mask_kind = kMaskTrie;
     p.out = e->attn; p.soh = D; p.som = static_cast<int64_t>(H) * D;
     p.sm_scale = 1.0f / sqrtf(static_cast<float>(D));
-    RB_TRY(attn_launch_engine(p, e->apart, e->max_chunks, st));
+    CUtensorMap tq;  // q buffer is [H, rows, 128]: its head stride depends on the bucket
+    RB_TRY(encode_heads_3d(&tq, e->qbuf, rows, H, D, static_cast<int64_t>(rows) * D));
+    RB_TRY(attn_launch_engine(p, e->apart, e->max_chunks, tq, e->m_kc[l], e->m_vc[l], st));
     // o projection + residual + post-attention norm
     g.epi = kEpiPartial;
     RB_TRY(gemm_launch_maps(s_o, e->m_attn, e->m_o[l], g, st));
@@ -391,10 +395,17 @@ int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
     }));
   }
   GemmLaunch gl{};
-  gl.epi = kEpiStoreF32;
-  gl.out = e->logits;
-  gl.ldo = c.vocab;
-  RB_TRY(gemm_launch_maps(s_lm, e->m_xn, e->m_lm, gl, st));
+  if (s_lm.splits == 1) {
+    gl.epi = kEpiStoreF32;
+    gl.out = e->logits;
+    gl.ldo = c.vocab;
+    RB_TRY(gemm_launch_maps(s_lm, e->m_xn, e->m_lm, gl, st));
+  } else {  // small vocabularies: split-K like rb_linear, fixed-order fp32 reduce
+    gl.epi = kEpiPartial;
+    gl.partial = e->part;
+    RB_TRY(gemm_launch_maps(s_lm, e->m_xn, e->m_lm, gl, st));
+    RB_TRY(splitk_reduce(e->part, s_lm.splits, rows, c.vocab, e->logits, c.vocab, 1, st));
+  }
   greedy_step_kernel<<<rows, 1024, 0, st>>>(e->d_params, e->logits, c.vocab, c.vocab, e->d_out);
   return check_launch();
 }
@@ -463,6 +474,8 @@ int rb_engine_create(const rb_model_config* cfg, const rb_model_weights* w, void
   e->m_o.resize(c.n_layers);
   e->m_gu.resize(c.n_layers);
   e->m_d.resize(c.n_layers);
+  e->m_kc.resize(c.n_layers);
+  e->m_vc.resize(c.n_layers);
   for (int l = 0; l < c.n_layers && st == RB_OK; ++l) {
     const rb_layer_weights& lw = e->layers[l];
     if (!lw.wqkv || !lw.wo || !lw.wgu || !lw.wd || !lw.in_norm || !lw.post_norm || !lw.q_norm || !lw.k_norm ||
@@ -474,6 +487,9 @@ int rb_engine_create(const rb_model_config* cfg, const rb_model_weights* w, void
     st |= gemm_encode_w(&e->m_o[l], lw.wo, c.hidden, c.n_heads * c.head_dim, c.n_heads * c.head_dim, s_o.BN);
     st |= gemm_encode_w(&e->m_gu[l], lw.wgu, 2 * c.ffn, c.hidden, c.hidden, 256);
     st |= gemm_encode_w(&e->m_d[l], lw.wd, c.hidden, c.ffn, c.ffn, s_d.BN);
+    const int64_t sh = static_cast<int64_t>(c.max_slots) * c.head_dim;
+    st |= encode_heads_3d(&e->m_kc[l], e->kc[l], c.max_slots, c.n_kv_heads, c.head_dim, sh);
+    st |= encode_heads_3d(&e->m_vc[l], e->vc[l], c.max_slots, c.n_kv_heads, c.head_dim, sh);
   }
   if (st == RB_OK) st = gemm_encode_w(&e->m_lm, w->lm_head, c.vocab, c.hidden, c.hidden, s_lm.BN);
   if (st != RB_OK) {

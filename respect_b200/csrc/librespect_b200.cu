@@ -3,6 +3,7 @@
 // relocatable device code.
 #include "host_util.cu"
 #include "gemm.cu"
+#include "attention_tc.cu"
 #include "attention.cu"
 #include "elementwise.cu"
 #include "capi.cu"
