@@ -48,7 +48,7 @@ def trie_with_path(rng, path_tokens, n_nodes, vocab, n_chains=4):
 @pytest.fixture(scope="module")
 def tiny():
     cfg = DecoderConfig.tiny(2)
-    w = DecoderWeights.random(cfg, DEV, seed=1, std=0.05)
+    w = DecoderWeights.random(cfg, DEV, seed=1, std=0.02)
     eng = VerifyEngine(w, max_rows=128, max_slots=1024)
     yield cfg, w, eng
     eng.close()
@@ -67,7 +67,8 @@ def test_tiny_engine_matches_oracle(tiny):
     vc = [np.zeros_like(k) for k in kc]
     omodel.prefill(W, omodel.cfg_dict(cfg), prompt, kc, vc, chunk=64)
     ref = omodel.verify_step(W, omodel.cfg_dict(cfg), tree.tokens(), tree.parents(), tree.depths(), 200, 0, kc, vc)
-    assert np.abs(got - ref).max() < 2e-2
+    err = np.abs(got - ref)
+    assert err.max() < 2e-2, (err.max(), np.abs(ref).max(), err.mean())
     ids = eng.next_ids(len(tree.nodes)).cpu().numpy()
     ref_ids = ref.argmax(-1)
     srt = np.sort(ref, axis=-1)

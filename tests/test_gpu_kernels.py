@@ -178,7 +178,10 @@ def test_rmsnorm_vs_oracle_and_row_invariance(N):
     y = rmsnorm(T(x, torch.bfloat16), T(w, torch.bfloat16), 1e-6)
     ref = oops.rmsnorm(x, w, 1e-6, bf16=True)
     got = y.float().cpu().numpy()
-    assert np.all(np.abs(got - ref) <= np.abs(ref) * 2 ** -7 + 1e-7)
+    # x*rsqrt is rounded to bf16, then w*x̂ again: one-ulp differences in the
+    # first rounding (rsqrtf vs exact) can become two ulps in the output.
+    assert np.all(np.abs(got - ref) <= np.abs(ref) * 2 ** -6 + 1e-7)
+    assert (got != ref).mean() < 0.02
     assert torch.equal(rmsnorm(T(x[:1], torch.bfloat16), T(w, torch.bfloat16), 1e-6), y[:1])
     yf = rmsnorm(T(x), T(w), 1e-6)
     assert np.abs(yf.cpu().numpy() - oops.rmsnorm(x, w, 1e-6, bf16=False)).max() < 1e-5
