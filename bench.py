@@ -40,7 +40,7 @@ PROMPT = 3000
 NODES = 128
 CHAIN = 32
 KERNELS_PER_LAYER = 9          # qkv gemm, qkv finish, attn prefix, attn nodes, o gemm, resid, gu gemm, down gemm, resid
-KERNELS_FIXED = 3              # embed+norm, lm_head gemm, greedy
+KERNELS_FIXED = 3              # embed+norm, lm_head gemm (+ greedy keys), greedy finalize
 
 
 def parse():

@@ -137,29 +137,56 @@ __device__ __forceinline__ bool node_allowed(const AttnDev& p, int row, int j) {
   }
 }
 
-// Fold node slot j into (m, l, acc): score by a fixed warp tree (every lane
-// takes lane 0's sum), then the online-softmax update, all fp32. This is the
-// only place node slots enter a row, whatever the masking mode.
+// Fold up to 8 node slots into (m, l, acc), in the order given. Scores are
+// computed for the whole batch first (the 8 warp trees interleave), then the
+// online-softmax updates run one slot at a time:
+//   s = (q.k) by a fixed warp tree, lane 0's sum broadcast, times scale*log2(e)
+//   m' = max(m, s); a = 2^(m - m'); p = 2^(s - m'); acc = p*v + acc*a; l = l*a + p
+// Every slot goes through exactly this arithmetic whatever the masking mode or
+// batch boundaries, so a row's bits depend only on its allowed slots' order.
+constexpr int kNodeBatch = 8;
+
 template <typename T>
-__device__ __forceinline__ void fold_node(const AttnDev& p, const T* kn, const T* vn, int kvh, int j,
-                                          const float (&qv)[4], int d0, float scale2, float& m, float& l,
-                                          float (&acc)[4]) {
-  float kv[4], vv[4];
-  ld4(kn + kvh * p.sknh + static_cast<int64_t>(j) * p.sknn + d0, kv);
-  ld4(vn + kvh * p.svnh + static_cast<int64_t>(j) * p.svnn + d0, vv);
-  float s = qv[0] * kv[0];
-  s = fmaf(qv[1], kv[1], s);
-  s = fmaf(qv[2], kv[2], s);
-  s = fmaf(qv[3], kv[3], s);
-  s = warp_sum(s);
-  s = __shfl_sync(0xffffffffu, s, 0) * scale2;
-  const float m_new = fmaxf(m, s);
-  const float a = fast_exp2(m - m_new);
-  const float pe = fast_exp2(s - m_new);
+__device__ __forceinline__ void fold_batch(const AttnDev& p, const T* kn, const T* vn, int kvh,
+                                           const int (&slot)[kNodeBatch], int cnt, const float (&qv)[4], int d0,
+                                           float scale2, float& m, float& l, float (&acc)[4]) {
+  float kv[kNodeBatch][4], vv[kNodeBatch][4], s[kNodeBatch];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) acc[e] = fmaf(pe, vv[e], acc[e] * a);
-  l = fmaf(l, a, pe);
-  m = m_new;
+  for (int u = 0; u < kNodeBatch; ++u) {
+    if (u < cnt) {
+      ld4(kn + kvh * p.sknh + static_cast<int64_t>(slot[u]) * p.sknn + d0, kv[u]);
+      ld4(vn + kvh * p.svnh + static_cast<int64_t>(slot[u]) * p.svnn + d0, vv[u]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) kv[u][e] = vv[u][e] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kNodeBatch; ++u) {
+    float t = qv[0] * kv[u][0];
+    t = fmaf(qv[1], kv[u][1], t);
+    t = fmaf(qv[2], kv[u][2], t);
+    t = fmaf(qv[3], kv[u][3], t);
+    s[u] = t;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int u = 0; u < kNodeBatch; ++u) s[u] += __shfl_xor_sync(0xffffffffu, s[u], o);
+  }
+#pragma unroll
+  for (int u = 0; u < kNodeBatch; ++u) {
+    if (u < cnt) {
+      const float su = __shfl_sync(0xffffffffu, s[u], 0) * scale2;
+      const float m_new = fmaxf(m, su);
+      const float a = fast_exp2(m - m_new);
+      const float pe = fast_exp2(su - m_new);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] = fmaf(pe, vv[u][e], acc[e] * a);
+      l = fmaf(l, a, pe);
+      m = m_new;
+    }
+  }
 }
 
 constexpr int kMaxTrieDepth = 1024;
@@ -213,11 +240,11 @@ __global__ void __launch_bounds__(128) attn_nodes(const AttnDev p, const float* 
   }
 
   const float scale2 = p.sm_scale * kLog2e;
+  int slot[kNodeBatch];
   if (p.mask_kind == kMaskTrie) {
     // Committed slots, in order, then the ancestors-or-self of this node in
     // increasing index (= slot) order; every other slot is masked.
     const int base = p.sp ? p.sp->base : p.causal_first;
-    for (int j = 0; j < base; ++j) fold_node<T>(p, kn, vn, kvh, j, qv, d0, scale2, m, l, acc);
     int depth = p.depths[row];
     if (depth < 0 || depth >= kMaxTrieDepth) {
       raise_device_error(0x201);
@@ -238,19 +265,33 @@ __global__ void __launch_bounds__(128) attn_nodes(const AttnDev p, const float* 
     }
     depth = __shfl_sync(0xffffffffu, depth, 0);
     __syncwarp();
-    for (int t = 0; t <= depth; ++t) fold_node<T>(p, kn, vn, kvh, base + chain[warp][t], qv, d0, scale2, m, l, acc);
+    const int total = base + depth + 1;
+    for (int b0 = 0; b0 < total; b0 += kNodeBatch) {
+      const int cnt = min(kNodeBatch, total - b0);
+#pragma unroll
+      for (int u = 0; u < kNodeBatch; ++u) {
+        const int i = b0 + u;
+        slot[u] = i < base ? i : (i < total ? base + chain[warp][i - base] : 0);
+      }
+      fold_batch<T>(p, kn, vn, kvh, slot, cnt, qv, d0, scale2, m, l, acc);
+    }
   } else {
     // Node slots in slot order, allowed ones only (a masked slot is an exact no-op).
+    int cnt = 0;
     for (int j0 = 0; j0 < p.NN; j0 += 32) {
       const int j = j0 + lane;
       const bool allow = j < p.NN && node_allowed(p, row, j);
       unsigned bits = __ballot_sync(0xffffffffu, allow);
       while (bits) {
-        const int jj = j0 + __ffs(bits) - 1;
+        slot[cnt++] = j0 + __ffs(bits) - 1;
         bits &= bits - 1;
-        fold_node<T>(p, kn, vn, kvh, jj, qv, d0, scale2, m, l, acc);
+        if (cnt == kNodeBatch) {
+          fold_batch<T>(p, kn, vn, kvh, slot, cnt, qv, d0, scale2, m, l, acc);
+          cnt = 0;
+        }
       }
     }
+    if (cnt) fold_batch<T>(p, kn, vn, kvh, slot, cnt, qv, d0, scale2, m, l, acc);
   }
 #pragma unroll
   for (int e = 0; e < 4; ++e) {

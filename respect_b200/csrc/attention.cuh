@@ -12,7 +12,7 @@ namespace rb {
 // Prefix keys are reduced in chunks of this many keys at absolute positions
 // [c*kPrefixChunk, (c+1)*kPrefixChunk). A compile-time constant: results of a
 // row depend on it, so it must never vary with the call.
-constexpr int kPrefixChunk = 512;
+constexpr int kPrefixChunk = 1024;
 // Per (chunk, head, row) partial: acc[128], max (log2 domain), sum, 2 pad.
 constexpr int kPartStride = 128 + 4;
 

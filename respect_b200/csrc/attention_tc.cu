@@ -8,9 +8,11 @@
 //   O = bf16(p) V        tcgen05.mma, A = P (smem, K-major), B = V (MN-major)
 //   acc = acc*alpha + O; l = l*alpha + sum(p)     (fp32, one row per thread)
 //
-// Warp roles: warps 0-3 softmax / correction (thread = query row = TMEM lane),
-// warp 4 TMA producer (Q once, K/V double-buffered), warp 5 MMA issuer and
-// TMEM owner. Each row's result depends only on that row and the chunk's keys:
+// Warp roles: warps 0-7 softmax / correction (two threads per query row: warp
+// w serves TMEM lanes 32*(w%4).., key / dim columns [64*(w/4), 64*(w/4)+64);
+// the row max and row sum of the halves are combined through shared memory,
+// lower half first), warp 8 TMA producer (Q once, K/V double-buffered), warp 9
+// MMA issuer and TMEM owner. Each row's result depends only on that row and the chunk's keys:
 // the MMA computes rows independently and every row reduction runs in a
 // fixed order, so a row gives the same bits whatever the other rows are.
 #include "attention.cuh"
@@ -27,8 +29,12 @@ constexpr int kKVOff = 2 * kHalf;            // 2 stages x (K 2 halves, V 2 halv
 constexpr int kStage = 4 * kHalf;            // 64 KB
 constexpr int kPOff = kKVOff + 2 * kStage;   // P: 2 halves (keys 0-63 | 64-127)
 constexpr int kBarOff = kPOff + 2 * kHalf;   // 192 KB
-constexpr int kSmem = 1024 + kBarOff + 256;
-constexpr int kThreads = 192;
+constexpr int kRedOff = kBarOff + 256;       // row max / row sum exchange: 2 x 2 x 128 floats
+constexpr int kSmem = 1024 + kRedOff + 512 * 4;
+static_assert(kSmem <= 232448, "shared memory budget");
+constexpr int kSoftmaxThreads = 256;
+constexpr int kThreads = kSoftmaxThreads + 64;
+constexpr int kProducerWarp = 8, kMmaWarp = 9;
 // barrier indices
 enum { Q_FULL = 0, KV_FULL = 1, KV_EMPTY = 3, S_FULL = 5, P_FULL = 7, O_FULL = 8, O_FREE = 9, NBAR = 10 };
 constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, 0, 0);
@@ -66,12 +72,12 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     mbar_init(bar(KV_EMPTY + 1), 1);
     mbar_init(bar(S_FULL), 1);
     mbar_init(bar(S_FULL + 1), 1);
-    mbar_init(bar(P_FULL), 128);
+    mbar_init(bar(P_FULL), kSoftmaxThreads);
     mbar_init(bar(O_FULL), 1);
-    mbar_init(bar(O_FREE), 128);
+    mbar_init(bar(O_FREE), kSoftmaxThreads);
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -81,7 +87,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t sQ = smem_u32(smem + kQOff), sKV = smem_u32(smem + kKVOff), sP = smem_u32(smem + kPOff);
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     if (lane == 0) {  // TMA producer
       const uint64_t pol = policy_evict_last();
       mbar_arrive_expect_tx(bar(Q_FULL), 2 * kHalf);
@@ -99,7 +105,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         tma_load_3d(st + 3 * kHalf, &tv, bar(KV_FULL + s), 64, key, kvh, pol);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     if (lane == 0) {  // MMA issuer
       auto issue_qk = [&](int j) {
         const uint32_t st = sKV + (j & 1) * kStage;
@@ -137,65 +143,69 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       }
     }
   } else {
-    // Softmax / correction: thread = row (TMEM lane 32*warp + lane).
-    const int r = threadIdx.x;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    // Softmax / correction. Thread (warp w, lane): row r = 32*(w%4) + lane,
+    // columns [64*hf, 64*hf + 64) of S (keys) and of O (dims), hf = w / 4.
+    const int q4 = warp & 3, hf = warp >> 2;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+    float* red = reinterpret_cast<float*>(smem + kRedOff);  // [2 (max|sum)][2 (half)][128] floats
     const float scale2 = p.sm_scale * 1.4426950408889634f;
     float m = -INFINITY, l = 0.f;
-    float acc[kD];
+    float acc[64];
 #pragma unroll
-    for (int i = 0; i < kD; ++i) acc[i] = 0.f;
+    for (int i = 0; i < 64; ++i) acc[i] = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       ok = __all_sync(0xffffffffu, mbar_wait(bar(S_FULL + (j & 1)), (j >> 1) & 1, 0x217));
       if (!ok) break;
       tc_fence_after();
-      const uint32_t sb = lane_base + (j & 1) * 128;
-      const int nvalid = min(kKeys, k1 - (k0 + j * kKeys));
+      const uint32_t sb = lane_base + (j & 1) * 128 + hf * 64;
+      const int nvalid = min(kKeys, k1 - (k0 + j * kKeys)) - hf * 64;  // valid keys in this half (may be <= 0)
+      uint32_t raw[4][16];
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) tmem_ld16_nowait(sb + cc * 16, raw[cc]);
+      tmem_wait_ld();
+      float sv[64];
       float mx = -INFINITY;
 #pragma unroll
-      for (int cc = 0; cc < kKeys / 16; ++cc) {
-        float v[16];
-        tmem_ld16(sb + cc * 16, v);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) mx = fmaxf(mx, cc * 16 + i < nvalid ? v[i] * scale2 : -INFINITY);
+      for (int i = 0; i < 64; ++i) {
+        sv[i] = i < nvalid ? __uint_as_float(raw[i >> 4][i & 15]) * scale2 : -INFINITY;
+        mx = fmaxf(mx, sv[i]);
       }
-      const float m_new = fmaxf(m, mx);
+      red[hf * 128 + r] = mx;
+      named_bar(1, kSoftmaxThreads);
+      mx = fmaxf(red[r], red[128 + r]);
+      const float m_new = fmaxf(m, mx);  // finite: every tile has a valid key in its lower half
       const float alpha = fast_exp2(m - m_new);
       float rs = 0.f;
+      uint8_t* rowp = smem + kPOff + hf * kHalf + r * 128;
 #pragma unroll
-      for (int cc = 0; cc < kKeys / 16; ++cc) {
-        float v[16];
-        tmem_ld16(sb + cc * 16, v);
-        uint32_t w[8];
+      for (int cc = 0; cc < 8; ++cc) {  // 8 keys = one 16-byte chunk of the swizzled row
+        uint32_t w[4];
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          const float p0 = cc * 16 + i < nvalid ? fast_exp2(v[i] * scale2 - m_new) : 0.f;
-          const float p1 = cc * 16 + i + 1 < nvalid ? fast_exp2(v[i + 1] * scale2 - m_new) : 0.f;
+        for (int i = 0; i < 8; i += 2) {
+          const float p0 = fast_exp2(sv[cc * 8 + i] - m_new);
+          const float p1 = fast_exp2(sv[cc * 8 + i + 1] - m_new);
           rs += p0;
           rs += p1;
           w[i / 2] = pack_bf16x2(p0, p1);
         }
-        // keys cc*16 .. cc*16+15 = two 16-byte chunks of the 128-byte swizzled row
-        const int half = cc >> 2, ch = (cc & 3) * 2;
-        uint8_t* rowp = smem + kPOff + half * kHalf + r * 128;
-        *reinterpret_cast<uint4*>(rowp + (((ch) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4*>(rowp + (((ch + 1) ^ (r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+        *reinterpret_cast<uint4*>(rowp + ((cc ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      l = fmaf(l, alpha, rs);
+      red[256 + hf * 128 + r] = rs;
       fence_proxy_async_smem();  // P stores -> visible to the tensor core (async proxy)
       tc_fence_before();         // S loads of this tile ordered before the arrive
       mbar_arrive(bar(P_FULL));
+      named_bar(1, kSoftmaxThreads);
+      l = fmaf(l, alpha, red[256 + r] + red[384 + r]);
       ok = __all_sync(0xffffffffu, mbar_wait(bar(O_FULL), j & 1, 0x218));
       if (!ok) break;
       tc_fence_after();
 #pragma unroll
-      for (int cc = 0; cc < kD / 16; ++cc) {
-        float o[16];
-        tmem_ld16(lane_base + 256 + cc * 16, o);
+      for (int cc = 0; cc < 4; ++cc) tmem_ld16_nowait(lane_base + 256 + hf * 64 + cc * 16, raw[cc]);
+      tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc[cc * 16 + i] = fmaf(acc[cc * 16 + i], alpha, o[i]);
-      }
+      for (int i = 0; i < 64; ++i) acc[i] = fmaf(acc[i], alpha, __uint_as_float(raw[i >> 4][i & 15]));
       tc_fence_before();
       mbar_arrive(bar(O_FREE));
       m = m_new;
@@ -204,14 +214,17 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     if (ok && row < M) {
       float* o = part + ((static_cast<int64_t>(c) * p.H + h) * p.M + row) * kPartStride;
 #pragma unroll
-      for (int i = 0; i < kD; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
-      o[kD] = m;
-      o[kD + 1] = l;
+      for (int i = 0; i < 64; i += 4)
+        *reinterpret_cast<float4*>(o + hf * 64 + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+      if (hf == 0) {
+        o[kD] = m;
+        o[kD + 1] = l;
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

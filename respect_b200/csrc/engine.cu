@@ -50,8 +50,8 @@ __device__ __forceinline__ float row_inv_rms(const float* v, int cnt, int N, flo
 
 constexpr int kMaxPerThread = 32;  // hidden <= 32 * NT
 
-// h[row] = embed[ids[row]];  xn[row] = rmsnorm(h[row], w)
-template <int NT>
+// h[row] = embed[ids[row]];  xn[row] = rmsnorm(h[row], w). EPT: elements per thread.
+template <int NT, int EPT>
 __global__ void __launch_bounds__(NT) embed_norm_kernel(const StepParams* __restrict__ sp, const int32_t* __restrict__ ids,
                                                         const uint16_t* __restrict__ emb, const uint16_t* __restrict__ w,
                                                         uint16_t* __restrict__ h, uint16_t* __restrict__ xn, int N,
@@ -65,23 +65,32 @@ __global__ void __launch_bounds__(NT) embed_norm_kernel(const StepParams* __rest
     id = 0;
   }
   const uint16_t* er = emb + static_cast<int64_t>(id) * N;
-  float v[kMaxPerThread];
-  int cnt = 0;
-  for (int i = threadIdx.x; i < N; i += NT) {
-    const uint16_t b = er[i];
-    h[static_cast<int64_t>(row) * N + i] = b;
-    v[cnt++] = bf16_bits_to_f32(b);
+  float v[EPT];
+#pragma unroll
+  for (int k = 0; k < EPT; ++k) {
+    const int i = threadIdx.x + k * NT;
+    v[k] = 0.f;
+    if (i < N) {
+      const uint16_t b = er[i];
+      h[static_cast<int64_t>(row) * N + i] = b;
+      v[k] = bf16_bits_to_f32(b);
+    }
   }
-  const float r = row_inv_rms<NT>(v, cnt, N, eps, red);
-  cnt = 0;
-  for (int i = threadIdx.x; i < N; i += NT) {
-    const float xh = round_bf16(v[cnt++] * r);
-    xn[static_cast<int64_t>(row) * N + i] = f32_to_bf16_bits(bf16_bits_to_f32(w[i]) * xh);
+  const float r = row_inv_rms<NT>(v, EPT, N, eps, red);
+#pragma unroll
+  for (int k = 0; k < EPT; ++k) {
+    const int i = threadIdx.x + k * NT;
+    if (i < N) {
+      const float xh = round_bf16(v[k] * r);
+      xn[static_cast<int64_t>(row) * N + i] = f32_to_bf16_bits(bf16_bits_to_f32(w[i]) * xh);
+    }
   }
 }
 
 // o = bf16(sum_s partial[s]);  h = bf16(h + o);  xn = rmsnorm(h, w)
-template <int NT>
+// Splits are summed in ascending order (as splitk_reduce does); the split loop
+// is outermost so every split's loads of a thread are in flight together.
+template <int NT, int EPT>
 __global__ void __launch_bounds__(NT) resid_norm_kernel(const StepParams* __restrict__ sp, const float* __restrict__ part,
                                                         int splits, int M, uint16_t* __restrict__ h,
                                                         const uint16_t* __restrict__ w, uint16_t* __restrict__ xn, int N,
@@ -90,23 +99,36 @@ __global__ void __launch_bounds__(NT) resid_norm_kernel(const StepParams* __rest
   const int row = blockIdx.x;
   if (row >= sp->q) return;
   const int64_t plane = static_cast<int64_t>(M) * N;
-  float v[kMaxPerThread];
-  int cnt = 0;
-  for (int i = threadIdx.x; i < N; i += NT) {
-    const float* p = part + static_cast<int64_t>(row) * N + i;
-    float acc = p[0];
-    for (int s = 1; s < splits; ++s) acc += p[s * plane];
-    const float o = round_bf16(acc);
-    const int64_t idx = static_cast<int64_t>(row) * N + i;
-    const float hn = round_bf16(bf16_bits_to_f32(h[idx]) + o);
-    h[idx] = f32_to_bf16_bits(hn);
-    v[cnt++] = hn;
+  const float* p = part + static_cast<int64_t>(row) * N + threadIdx.x;
+  float acc[EPT];
+#pragma unroll
+  for (int k = 0; k < EPT; ++k) acc[k] = (threadIdx.x + k * NT < N) ? p[k * NT] : 0.f;
+  for (int s = 1; s < splits; ++s) {
+    const float* ps = p + s * plane;
+#pragma unroll
+    for (int k = 0; k < EPT; ++k)
+      if (threadIdx.x + k * NT < N) acc[k] += ps[k * NT];
   }
-  const float r = row_inv_rms<NT>(v, cnt, N, eps, red);
-  cnt = 0;
-  for (int i = threadIdx.x; i < N; i += NT) {
-    const float xh = round_bf16(v[cnt++] * r);
-    xn[static_cast<int64_t>(row) * N + i] = f32_to_bf16_bits(bf16_bits_to_f32(w[i]) * xh);
+  float v[EPT];
+#pragma unroll
+  for (int k = 0; k < EPT; ++k) {
+    const int i = threadIdx.x + k * NT;
+    v[k] = 0.f;
+    if (i < N) {
+      const int64_t idx = static_cast<int64_t>(row) * N + i;
+      const float hn = round_bf16(bf16_bits_to_f32(h[idx]) + round_bf16(acc[k]));
+      h[idx] = f32_to_bf16_bits(hn);
+      v[k] = hn;
+    }
+  }
+  const float r = row_inv_rms<NT>(v, EPT, N, eps, red);
+#pragma unroll
+  for (int k = 0; k < EPT; ++k) {
+    const int i = threadIdx.x + k * NT;
+    if (i < N) {
+      const float xh = round_bf16(v[k] * r);
+      xn[static_cast<int64_t>(row) * N + i] = f32_to_bf16_bits(bf16_bits_to_f32(w[i]) * xh);
+    }
   }
 }
 
@@ -128,13 +150,15 @@ __global__ void __launch_bounds__(128) qkv_finish_kernel(
   const int N = nh * D;
   const int64_t plane = static_cast<int64_t>(M) * N;
   float x[4];
+  const float* p = part + static_cast<int64_t>(row) * N + head * D + lane;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float* p = part + static_cast<int64_t>(row) * N + head * D + lane + 32 * k;
-    float acc = p[0];
-    for (int s = 1; s < splits; ++s) acc += p[s * plane];
-    x[k] = round_bf16(acc);
+  for (int k = 0; k < 4; ++k) x[k] = p[32 * k];
+  for (int s = 1; s < splits; ++s) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) x[k] += p[s * plane + 32 * k];
   }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) x[k] = round_bf16(x[k]);
   const int slot = sp->prompt_len + sp->base + row;
   if (slot >= max_slots) {
     raise_device_error(0x302);
@@ -179,36 +203,29 @@ __global__ void __launch_bounds__(128) qkv_finish_kernel(
   for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = f32_to_bf16_bits(o[k]);
 }
 
-// Greedy choice of the live rows, reading the excluded range from the params.
-__global__ void greedy_step_kernel(const StepParams* __restrict__ sp, const float* __restrict__ logits, int64_t ld,
-                                   int V, int64_t* __restrict__ out) {
-  const int row = blockIdx.x;
+// Greedy ids of the live rows from the per-row keys the lm_head epilogue (or
+// the small-vocabulary path below) folded with atomicMax.
+__global__ void greedy_finalize_kernel(const StepParams* __restrict__ sp, const unsigned long long* __restrict__ keys,
+                                       int64_t* __restrict__ out, int rows) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows || row >= sp->q) return;
+  const unsigned long long k = keys[row];
+  out[row] = k ? static_cast<int64_t>(0xFFFFFFFFu - static_cast<unsigned int>(k & 0xFFFFFFFFu)) : 0;
+}
+
+// Small vocabularies (lm_head split over K): the same keys from the reduced logits.
+__global__ void argmax_keys_kernel(const StepParams* __restrict__ sp, const float* __restrict__ logits, int64_t ld,
+                                   int V, unsigned long long* __restrict__ keys) {
+  const int row = blockIdx.y;
   if (row >= sp->q) return;
-  const float* r = logits + static_cast<int64_t>(row) * ld;
-  const int off = sp->act_off, size = sp->act_size;
-  float bv = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    if (i >= off && i < off + size) continue;
-    const float v = r[i];
-    if (better(v, i, bv, bi)) { bv = v; bi = i; }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
-  }
-  __shared__ float sv[32];
-  __shared__ int si[32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
-      if (better(sv[w], si[w], bv, bi)) { bv = sv[w]; bi = si[w]; }
-    out[row] = (bi == 0x7fffffff) ? 0 : bi;
-  }
+  const int ex0 = sp->act_off, ex1 = sp->act_off + sp->act_size;
+  unsigned long long best = 0;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x)
+    if (i < ex0 || i >= ex1) {
+      const unsigned long long k = argmax_key(logits[static_cast<int64_t>(row) * ld + i], i);
+      best = k > best ? k : best;
+    }
+  if (best) atomicMax(keys + row, best);
 }
 
 }  // namespace rb
@@ -229,6 +246,7 @@ struct rb_engine {
   int64_t* d_out = nullptr;
   uint16_t *h = nullptr, *xn = nullptr, *qbuf = nullptr, *attn = nullptr, *act = nullptr;
   float *part = nullptr, *apart = nullptr, *logits = nullptr;
+  unsigned long long* keys = nullptr;
   int max_chunks = 1;
   // tensor maps
   CUtensorMap m_xn, m_attn, m_act, m_lm;
@@ -251,7 +269,7 @@ constexpr int kQkvNT = 128;
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
-  size_t params, ids, parents, depths, out, h, xn, qbuf, attn, act, part, apart, logits, total;
+  size_t params, ids, parents, depths, out, keys, h, xn, qbuf, attn, act, part, apart, logits, total;
 };
 
 Layout layout_of(const rb_model_config& c) {
@@ -275,6 +293,7 @@ Layout layout_of(const rb_model_config& c) {
   L.parents = take(R * 4);
   L.depths = take(R * 4);
   L.out = take(R * 8);
+  L.keys = take(R * 8);
   L.h = take(R * c.hidden * 2);
   L.xn = take(R * c.hidden * 2);
   L.qbuf = take(static_cast<size_t>(c.n_heads) * R * c.head_dim * 2);
@@ -299,11 +318,24 @@ int validate_cfg(const rb_model_config* c) {
   return RB_OK;
 }
 
+// Threads per row by N (the same choice as rmsnorm_kernel), elements per thread
+// rounded up to a power of two for a statically indexed register array.
+template <int NT, typename F>
+int launch_norm_ept(int N, F&& f) {
+  const int ept = (N + NT - 1) / NT;
+  if (ept <= 1) return f(std::integral_constant<int, NT>{}, std::integral_constant<int, 1>{});
+  if (ept <= 2) return f(std::integral_constant<int, NT>{}, std::integral_constant<int, 2>{});
+  if (ept <= 4) return f(std::integral_constant<int, NT>{}, std::integral_constant<int, 4>{});
+  if (ept <= 8) return f(std::integral_constant<int, NT>{}, std::integral_constant<int, 8>{});
+  if (ept <= 16) return f(std::integral_constant<int, NT>{}, std::integral_constant<int, 16>{});
+  if (ept <= 32) return f(std::integral_constant<int, NT>{}, std::integral_constant<int, 32>{});
+  return RB_ERR_UNSUPPORTED;
+}
 template <typename F>
 int launch_norm_nt(int N, F&& f) {
-  if (N >= 2048) return f(std::integral_constant<int, 256>{});
-  if (N >= 512) return f(std::integral_constant<int, 128>{});
-  return f(std::integral_constant<int, 32>{});
+  if (N >= 2048) return launch_norm_ept<256>(N, f);
+  if (N >= 512) return launch_norm_ept<128>(N, f);
+  return launch_norm_ept<32>(N, f);
 }
 
 #define RB_TRY(x)                     \
@@ -327,9 +359,9 @@ int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
   const GemmShape s_lm = gemm_plan(rows, c.vocab, hid, e->nsm);
   if (s_lm.BN != e->bn_lm) return RB_ERR_INVALID_ARG;
 
-  RB_TRY(launch_norm_nt(hid, [&](auto nt) {
-    constexpr int NT = decltype(nt)::value;
-    embed_norm_kernel<NT><<<rows, NT, 0, st>>>(e->d_params, e->d_ids, static_cast<const uint16_t*>(e->w.embed),
+  RB_TRY(launch_norm_nt(hid, [&](auto nt, auto ept) {
+    constexpr int NT = decltype(nt)::value, EPT = decltype(ept)::value;
+    embed_norm_kernel<NT, EPT><<<rows, NT, 0, st>>>(e->d_params, e->d_ids, static_cast<const uint16_t*>(e->w.embed),
                                                static_cast<const uint16_t*>(e->layers[0].in_norm), e->h, e->xn, hid,
                                                c.vocab, c.rms_eps);
     return check_launch();
@@ -371,9 +403,9 @@ int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
     // o projection + residual + post-attention norm
     g.epi = kEpiPartial;
     RB_TRY(gemm_launch_maps(s_o, e->m_attn, e->m_o[l], g, st));
-    RB_TRY(launch_norm_nt(hid, [&](auto nt) {
-      constexpr int NT = decltype(nt)::value;
-      resid_norm_kernel<NT><<<rows, NT, 0, st>>>(e->d_params, e->part, s_o.splits, rows, e->h,
+    RB_TRY(launch_norm_nt(hid, [&](auto nt, auto ept) {
+      constexpr int NT = decltype(nt)::value, EPT = decltype(ept)::value;
+      resid_norm_kernel<NT, EPT><<<rows, NT, 0, st>>>(e->d_params, e->part, s_o.splits, rows, e->h,
                                                  static_cast<const uint16_t*>(lw.post_norm), e->xn, hid, c.rms_eps);
       return check_launch();
     }));
@@ -387,26 +419,32 @@ int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
     g.epi = kEpiPartial;
     RB_TRY(gemm_launch_maps(s_d, e->m_act, e->m_d[l], g, st));
     const void* next_norm = (l + 1 < c.n_layers) ? e->layers[l + 1].in_norm : e->w.final_norm;
-    RB_TRY(launch_norm_nt(hid, [&](auto nt) {
-      constexpr int NT = decltype(nt)::value;
-      resid_norm_kernel<NT><<<rows, NT, 0, st>>>(e->d_params, e->part, s_d.splits, rows, e->h,
+    RB_TRY(launch_norm_nt(hid, [&](auto nt, auto ept) {
+      constexpr int NT = decltype(nt)::value, EPT = decltype(ept)::value;
+      resid_norm_kernel<NT, EPT><<<rows, NT, 0, st>>>(e->d_params, e->part, s_d.splits, rows, e->h,
                                                  static_cast<const uint16_t*>(next_norm), e->xn, hid, c.rms_eps);
       return check_launch();
     }));
   }
+  // lm_head (fp32 scores) with the greedy choice (acceptance.py:11-23) folded in.
+  if (cudaMemsetAsync(e->keys, 0, static_cast<size_t>(rows) * 8, st) != cudaSuccess) return RB_ERR_CUDA;
   GemmLaunch gl{};
   if (s_lm.splits == 1) {
-    gl.epi = kEpiStoreF32;
+    gl.epi = kEpiF32Argmax;
     gl.out = e->logits;
     gl.ldo = c.vocab;
+    gl.keys = e->keys;
+    gl.excl = &e->d_params->act_off;
     RB_TRY(gemm_launch_maps(s_lm, e->m_xn, e->m_lm, gl, st));
   } else {  // small vocabularies: split-K like rb_linear, fixed-order fp32 reduce
     gl.epi = kEpiPartial;
     gl.partial = e->part;
     RB_TRY(gemm_launch_maps(s_lm, e->m_xn, e->m_lm, gl, st));
     RB_TRY(splitk_reduce(e->part, s_lm.splits, rows, c.vocab, e->logits, c.vocab, 1, st));
+    argmax_keys_kernel<<<dim3(8, rows), 256, 0, st>>>(e->d_params, e->logits, c.vocab, c.vocab, e->keys);
+    RB_TRY(check_launch());
   }
-  greedy_step_kernel<<<rows, 1024, 0, st>>>(e->d_params, e->logits, c.vocab, c.vocab, e->d_out);
+  greedy_finalize_kernel<<<(rows + 127) / 128, 128, 0, st>>>(e->d_params, e->keys, e->d_out, rows);
   return check_launch();
 }
 
@@ -449,6 +487,7 @@ int rb_engine_create(const rb_model_config* cfg, const rb_model_weights* w, void
   e->d_parents = reinterpret_cast<int32_t*>(base + L.parents);
   e->d_depths = reinterpret_cast<int32_t*>(base + L.depths);
   e->d_out = reinterpret_cast<int64_t*>(base + L.out);
+  e->keys = reinterpret_cast<unsigned long long*>(base + L.keys);
   e->h = reinterpret_cast<uint16_t*>(base + L.h);
   e->xn = reinterpret_cast<uint16_t*>(base + L.xn);
   e->qbuf = reinterpret_cast<uint16_t*>(base + L.qbuf);

@@ -39,10 +39,12 @@ struct GemmKernelArgs {
   void* out;
   int64_t ldo;
   float* partial;
+  unsigned long long* keys;
+  const int* excl;
 };
 
 template <int EPI>
-__device__ __forceinline__ void epi_store16(const GemmKernelArgs& a, int m, int n0, int split,
+__device__ __forceinline__ void epi_store16_impl(const GemmKernelArgs& a, int m, int n0, int split,
                                             const float (&v)[16]) {
   if (EPI == kEpiStoreBF16) {
     uint16_t* o = static_cast<uint16_t*>(a.out) + static_cast<int64_t>(m) * a.ldo + n0;
@@ -79,6 +81,12 @@ __device__ __forceinline__ void epi_store16(const GemmKernelArgs& a, int m, int 
         if (n0 + i < a.N) o[i] = v[i];
     }
   }
+}
+
+template <int EPI>
+__device__ __forceinline__ void epi_store16(const GemmKernelArgs& a, int m, int n0, int split,
+                                            const float (&v)[16]) {
+  epi_store16_impl<EPI == kEpiF32Argmax ? kEpiStoreF32 : EPI>(a, m, n0, split, v);
 }
 
 // SiLU * mul with PyTorch eager rounding points: g, u are the bf16 GEMM
@@ -195,13 +203,29 @@ __global__ void __launch_bounds__(128, 1)
           }
         }
       } else {
+        unsigned long long best = 0;
+        int ex0 = 0, ex1 = 0;
+        if (EPI == kEpiF32Argmax) { ex0 = a.excl[0]; ex1 = ex0 + a.excl[1]; }
 #pragma unroll 1
         for (int c = 0; c < BN / 16; ++c) {
           float v[16];
           tmem_ld16(lane_base + mt * C::kAccStride + c * 16, v);
           const int n0 = n_tile * BN + c * 16;
-          if (m < a.M && n0 < a.N) epi_store16<EPI>(a, m, n0, split, v);
+          if (m < a.M && n0 < a.N) {
+            epi_store16<EPI>(a, m, n0, split, v);
+            if (EPI == kEpiF32Argmax) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int n = n0 + i;
+                if (n < a.N && (n < ex0 || n >= ex1)) {
+                  const unsigned long long k = argmax_key(v[i], n);
+                  best = k > best ? k : best;
+                }
+              }
+            }
+          }
         }
+        if (EPI == kEpiF32Argmax && m < a.M && best != 0) atomicMax(a.keys + m, best);
       }
     }
   }
@@ -276,6 +300,7 @@ static int launch_epi(const GemmShape& s, const CUtensorMap& mx, const CUtensorM
     case kEpiStoreF32: return launch_t<BN, MT, kEpiStoreF32>(s, mx, mw, ka, stream);
     case kEpiSiluMul: return launch_t<BN, MT, kEpiSiluMul>(s, mx, mw, ka, stream);
     case kEpiPartial: return launch_t<BN, MT, kEpiPartial>(s, mx, mw, ka, stream);
+    case kEpiF32Argmax: return launch_t<BN, MT, kEpiF32Argmax>(s, mx, mw, ka, stream);
   }
   return RB_ERR_INVALID_ARG;
 }
@@ -289,7 +314,10 @@ int gemm_launch_maps(const GemmShape& s, const CUtensorMap& mx, const CUtensorMa
   ka.out = a.out;
   ka.ldo = a.ldo;
   ka.partial = a.partial;
+  ka.keys = a.keys;
+  ka.excl = a.excl;
   if (a.epi == kEpiPartial ? a.partial == nullptr : a.out == nullptr) return RB_ERR_INVALID_ARG;
+  if (a.epi == kEpiF32Argmax && (!a.keys || !a.excl)) return RB_ERR_INVALID_ARG;
   if (a.epi != kEpiPartial && s.splits != 1) return RB_ERR_INVALID_ARG;
   if (a.epi == kEpiSiluMul && (s.N % s.BN) != 0) return RB_ERR_UNSUPPORTED;
   const int key = s.BN * 4 + s.mt;

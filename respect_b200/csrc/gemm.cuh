@@ -22,7 +22,28 @@ enum GemmEpilogue : int {
   kEpiStoreF32 = 1,   // out[m, n] = acc (lm_head scores)
   kEpiSiluMul = 2,    // W rows interleaved per BN block (gate | up): out[m, j] = bf16(bf16(silu(bf16 g)) * bf16 u)
   kEpiPartial = 3,    // partial[s, m, n] = acc (fp32, split-K)
+  kEpiF32Argmax = 4,  // kEpiStoreF32 + per-row greedy choice folded into keys[m] by atomicMax
 };
+
+// Order-preserving 64-bit key of (value, index): larger value first, then the
+// lower index; NaN above every number (torch.argmax). max() over keys is
+// associative and commutative, so the choice does not depend on tile order.
+__host__ __device__ inline unsigned long long argmax_key(float v, int idx) {
+  unsigned int u;
+  if (v != v) {
+    u = 0xFFFFFFFFu;
+  } else {
+    if (v == 0.0f) v = 0.0f;  // -0 and +0 compare equal: one key
+#ifdef __CUDA_ARCH__
+    u = __float_as_uint(v);
+#else
+    union { float f; unsigned int i; } c{v};
+    u = c.i;
+#endif
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  }
+  return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<unsigned int>(idx));
+}
 
 struct GemmShape {
   int M, N, K;
@@ -42,6 +63,8 @@ struct GemmLaunch {
   void* out; int64_t ldo;       // epilogue output
   float* partial;               // [splits, M, N] fp32 (kEpiPartial)
   int epi;
+  unsigned long long* keys;     // kEpiF32Argmax: [M] per-row keys (caller zeroes them)
+  const int* excl;              // kEpiF32Argmax: {offset, size} of the excluded column range (device)
 };
 
 // Encodes the tensor maps and launches. Returns an rb_status code.
