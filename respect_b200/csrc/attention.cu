@@ -49,6 +49,8 @@ __global__ void __launch_bounds__(128) attn_prefix_simt(const AttnDev p, float* 
   const int c = blockIdx.x, h = blockIdx.y, r0 = blockIdx.z * RB;
   const int kvh = h / (p.H / p.HK);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();
   const int NP = p.sp ? p.sp->prompt_len : p.NP;
   const int M = p.sp ? min(p.M, p.sp->q) : p.M;
   const int k0 = c * kPrefixChunk;
@@ -196,9 +198,18 @@ template <typename T>
 __global__ void __launch_bounds__(128) attn_nodes(const AttnDev p, const float* __restrict__ part) {
   constexpr int D = 128;
   __shared__ int chain[4][kMaxTrieDepth];
+  __shared__ int par_s[kMaxTrieDepth];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 4 + warp;
   const int h = blockIdx.y;
+  pdl_trigger();
+  pdl_wait();
+  if (p.mask_kind == kMaskTrie) {
+    // the block's rows walk their parent chains in shared memory
+    const int nq = min(p.sp ? p.sp->q : p.M, kMaxTrieDepth);
+    for (int i = threadIdx.x; i < nq; i += blockDim.x) par_s[i] = p.parents[i];
+    __syncthreads();
+  }
   if (row >= p.M) return;
   const int d0 = lane * 4;
   T* out = static_cast<T*>(p.out) + h * p.soh + static_cast<int64_t>(row) * p.som + d0;
@@ -246,7 +257,7 @@ __global__ void __launch_bounds__(128) attn_nodes(const AttnDev p, const float* 
     // increasing index (= slot) order; every other slot is masked.
     const int base = p.sp ? p.sp->base : p.causal_first;
     int depth = p.depths[row];
-    if (depth < 0 || depth >= kMaxTrieDepth) {
+    if (depth < 0 || depth >= kMaxTrieDepth || depth > row) {
       raise_device_error(0x201);
       depth = -1;
     }
@@ -254,7 +265,7 @@ __global__ void __launch_bounds__(128) attn_nodes(const AttnDev p, const float* 
       int a = row;
       for (int t = depth; t >= 0; --t) {
         chain[warp][t] = a;
-        const int par = p.parents[a];
+        const int par = par_s[a];
         if ((t > 0 && (par < 0 || par >= a)) || (t == 0 && par != -1)) {
           raise_device_error(0x202);  // parents / depths inconsistent: fold nothing more
           depth = -1;
@@ -367,7 +378,7 @@ int attn_launch(const rb_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t s
           encode_heads_3d(&tk, a->kp, a->NP, a->HK, a->skpn, a->skph) != RB_OK ||
           encode_heads_3d(&tv, a->vp, a->NP, a->HK, a->svpn, a->svph) != RB_OK)
         return RB_ERR_UNSUPPORTED;  // TMA needs 16-byte aligned bases and row strides
-      const int st = attn_prefix_tc_launch(tq, tk, tv, p, part, nchunks, stream);
+      const int st = attn_prefix_tc_launch(tq, tk, tv, p, part, nchunks, stream, false);
       if (st != RB_OK) return st;
     }
   }
@@ -380,11 +391,10 @@ int attn_launch(const rb_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t s
 // Engine path: bf16, q/base/PL from device memory, trie masking from parents.
 int attn_launch_engine(const AttnDev& p, float* part, int max_chunks, const CUtensorMap& tq,
                        const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t stream) {
-  const int st = attn_prefix_tc_launch(tq, tk, tv, p, part, max_chunks, stream);
+  const int st = attn_prefix_tc_launch(tq, tk, tv, p, part, max_chunks, stream, true);
   if (st != RB_OK) return st;
   dim3 grid2((p.M + 3) / 4, p.H);
-  attn_nodes<uint16_t><<<grid2, 128, 0, stream>>>(p, part);
-  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;
+  return launch_k(attn_nodes<uint16_t>, grid2, dim3(128), 0, stream, true, p, static_cast<const float*>(part));
 }
 
 }  // namespace rb

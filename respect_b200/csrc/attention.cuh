@@ -54,6 +54,6 @@ int attn_launch_engine(const AttnDev& p, float* part, int max_chunks, const CUte
 // 3-D tensor map of [heads, rows, 128] bf16 with 64 x 128 x 1 boxes (TMA, 128-byte swizzle).
 int encode_heads_3d(CUtensorMap* m, const void* base, int rows, int heads, int64_t ld_row, int64_t ld_head);
 int attn_prefix_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const AttnDev& p,
-                          float* part, int nchunks, cudaStream_t stream);
+                          float* part, int nchunks, cudaStream_t stream, bool pdl);
 
 }  // namespace rb

@@ -60,6 +60,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   const int ntiles = (k1 - k0 + kKeys - 1) / kKeys;
   const int kvh = h / (p.H / p.HK);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tq);
@@ -85,6 +86,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // q / K / V come from the previous kernels
   const uint32_t sQ = smem_u32(smem + kQOff), sKV = smem_u32(smem + kKVOff), sP = smem_u32(smem + kPOff);
 
   if (warp == kProducerWarp) {
@@ -240,13 +242,11 @@ int encode_heads_3d(CUtensorMap* m, const void* base, int rows, int heads, int64
 }
 
 int attn_prefix_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const AttnDev& p,
-                          float* part, int nchunks, cudaStream_t stream) {
-  static_assert(tc::kSmem <= 232448, "shared memory budget");
+                          float* part, int nchunks, cudaStream_t stream, bool pdl) {
   if (cudaFuncSetAttribute(attn_prefix_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmem) != cudaSuccess)
     return RB_ERR_CUDA;
   dim3 grid(nchunks, p.H, (p.M + tc::kRows - 1) / tc::kRows);
-  attn_prefix_tc<<<grid, tc::kThreads, tc::kSmem, stream>>>(tq, tk, tv, p, part);
-  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;
+  return launch_k(attn_prefix_tc, grid, dim3(tc::kThreads), tc::kSmem, stream, pdl, tq, tk, tv, p, part);
 }
 
 }  // namespace rb

@@ -232,6 +232,17 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn = 0
          | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
 }
 
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while its predecessor runs. Everything before
+// pdl_wait() must touch only memory the predecessor neither reads nor writes
+// (shared memory, TMEM, weights); pdl_wait() returns once the predecessor grid
+// has completed and its writes are visible. pdl_trigger() lets the successor
+// launch once every CTA of this grid has started. Both are no-ops for a
+// normal launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- warp utils
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

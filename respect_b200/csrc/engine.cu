@@ -58,6 +58,8 @@ __global__ void __launch_bounds__(NT) embed_norm_kernel(const StepParams* __rest
                                                         int vocab, float eps) {
   __shared__ float red[NT / 32];
   const int row = blockIdx.x;
+  pdl_trigger();
+  pdl_wait();
   if (row >= sp->q) return;
   int id = ids[row];
   if (id < 0 || id >= vocab) {
@@ -90,24 +92,31 @@ __global__ void __launch_bounds__(NT) embed_norm_kernel(const StepParams* __rest
 // o = bf16(sum_s partial[s]);  h = bf16(h + o);  xn = rmsnorm(h, w)
 // Splits are summed in ascending order (as splitk_reduce does); the split loop
 // is outermost so every split's loads of a thread are in flight together.
-template <int NT, int EPT>
+template <int NT, int EPT, int MAXS>
 __global__ void __launch_bounds__(NT) resid_norm_kernel(const StepParams* __restrict__ sp, const float* __restrict__ part,
                                                         int splits, int M, uint16_t* __restrict__ h,
                                                         const uint16_t* __restrict__ w, uint16_t* __restrict__ xn, int N,
                                                         float eps) {
   __shared__ float red[NT / 32];
   const int row = blockIdx.x;
+  pdl_trigger();
+  pdl_wait();
   if (row >= sp->q) return;
   const int64_t plane = static_cast<int64_t>(M) * N;
   const float* p = part + static_cast<int64_t>(row) * N + threadIdx.x;
   float acc[EPT];
 #pragma unroll
-  for (int k = 0; k < EPT; ++k) acc[k] = (threadIdx.x + k * NT < N) ? p[k * NT] : 0.f;
-  for (int s = 1; s < splits; ++s) {
-    const float* ps = p + s * plane;
+  for (int k = 0; k < EPT; ++k) {
+    // all splits' loads first (independent), then the sum in ascending split order
+    float t[MAXS];
+    const bool live = threadIdx.x + k * NT < N;
 #pragma unroll
-    for (int k = 0; k < EPT; ++k)
-      if (threadIdx.x + k * NT < N) acc[k] += ps[k * NT];
+    for (int s = 0; s < MAXS; ++s) t[s] = (live && s < splits) ? p[s * plane + k * NT] : 0.f;
+    float a = t[0];
+#pragma unroll
+    for (int s = 1; s < MAXS; ++s)
+      if (s < splits) a += t[s];
+    acc[k] = a;
   }
   float v[EPT];
 #pragma unroll
@@ -146,6 +155,8 @@ __global__ void __launch_bounds__(128) qkv_finish_kernel(
   const int row = blockIdx.x;
   const int head = blockIdx.y * 4 + warp;
   const int nh = H + 2 * HK;
+  pdl_trigger();
+  pdl_wait();
   if (row >= sp->q || head >= nh) return;
   const int N = nh * D;
   const int64_t plane = static_cast<int64_t>(M) * N;
@@ -205,11 +216,16 @@ __global__ void __launch_bounds__(128) qkv_finish_kernel(
 
 // Greedy ids of the live rows from the per-row keys the lm_head epilogue (or
 // the small-vocabulary path below) folded with atomicMax.
-__global__ void greedy_finalize_kernel(const StepParams* __restrict__ sp, const unsigned long long* __restrict__ keys,
+// Keys are reset to zero here, ready for the next step (zeroed once at set-up).
+__global__ void greedy_finalize_kernel(const StepParams* __restrict__ sp, unsigned long long* __restrict__ keys,
                                        int64_t* __restrict__ out, int rows) {
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= rows || row >= sp->q) return;
+  pdl_trigger();
+  pdl_wait();
+  if (row >= rows) return;
   const unsigned long long k = keys[row];
+  keys[row] = 0;
+  if (row >= sp->q) return;
   out[row] = k ? static_cast<int64_t>(0xFFFFFFFFu - static_cast<unsigned int>(k & 0xFFFFFFFFu)) : 0;
 }
 
@@ -217,6 +233,8 @@ __global__ void greedy_finalize_kernel(const StepParams* __restrict__ sp, const 
 __global__ void argmax_keys_kernel(const StepParams* __restrict__ sp, const float* __restrict__ logits, int64_t ld,
                                    int V, unsigned long long* __restrict__ keys) {
   const int row = blockIdx.y;
+  pdl_trigger();
+  pdl_wait();
   if (row >= sp->q) return;
   const int ex0 = sp->act_off, ex1 = sp->act_off + sp->act_size;
   unsigned long long best = 0;
@@ -346,6 +364,23 @@ int launch_norm_nt(int N, F&& f) {
 
 int check_launch() { return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA; }
 
+int launch_resid_norm(rb_engine* e, int splits, int rows, const void* w, cudaStream_t st) {
+  const rb_model_config& c = e->cfg;
+  return launch_norm_nt(c.hidden, [&](auto nt, auto ept) {
+    constexpr int NT = decltype(nt)::value, EPT = decltype(ept)::value;
+    auto go = [&](auto ms) {
+      constexpr int MAXS = decltype(ms)::value;
+      return launch_k(resid_norm_kernel<NT, EPT, MAXS>, dim3(rows), dim3(NT), 0, st, true,
+                      static_cast<const StepParams*>(e->d_params), static_cast<const float*>(e->part), splits, rows,
+                      e->h, static_cast<const uint16_t*>(w), e->xn, c.hidden, c.rms_eps);
+    };
+    if (splits <= 4) return go(std::integral_constant<int, 4>{});
+    if (splits <= 8) return go(std::integral_constant<int, 8>{});
+    if (splits <= 16) return go(std::integral_constant<int, 16>{});
+    return static_cast<int>(RB_ERR_UNSUPPORTED);
+  });
+}
+
 // Enqueue one verify step for `rows` (bucketed) query rows on `st`.
 int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
   const rb_model_config& c = e->cfg;
@@ -361,10 +396,10 @@ int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
 
   RB_TRY(launch_norm_nt(hid, [&](auto nt, auto ept) {
     constexpr int NT = decltype(nt)::value, EPT = decltype(ept)::value;
-    embed_norm_kernel<NT, EPT><<<rows, NT, 0, st>>>(e->d_params, e->d_ids, static_cast<const uint16_t*>(e->w.embed),
-                                               static_cast<const uint16_t*>(e->layers[0].in_norm), e->h, e->xn, hid,
-                                               c.vocab, c.rms_eps);
-    return check_launch();
+    return launch_k(embed_norm_kernel<NT, EPT>, dim3(rows), dim3(NT), 0, st, true,
+                    static_cast<const StepParams*>(e->d_params), static_cast<const int32_t*>(e->d_ids),
+                    static_cast<const uint16_t*>(e->w.embed), static_cast<const uint16_t*>(e->layers[0].in_norm),
+                    e->h, e->xn, hid, c.vocab, c.rms_eps);
   }));
   for (int l = 0; l < c.n_layers; ++l) {
     const rb_layer_weights& lw = e->layers[l];
@@ -372,15 +407,14 @@ int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
     // q|k|v projection
     g.epi = kEpiPartial;
     g.partial = e->part;
-    RB_TRY(gemm_launch_maps(s_qkv, e->m_xn, e->m_qkv[l], g, st));
+    RB_TRY(gemm_launch_maps(s_qkv, e->m_xn, e->m_qkv[l], g, st, true));
     dim3 gq(rows, (H + 2 * HK + 3) / 4);
-    qkv_finish_kernel<<<gq, kQkvNT, 0, st>>>(
-        e->d_params, e->d_depths, e->part, s_qkv.splits, rows, H, HK, static_cast<const uint16_t*>(lw.q_norm),
-        static_cast<const uint16_t*>(lw.k_norm), static_cast<const uint16_t*>(e->w.rope_cos),
-        static_cast<const uint16_t*>(e->w.rope_sin), c.max_pos, c.rms_eps, e->qbuf,
-        static_cast<uint16_t*>(e->kc[l]), static_cast<uint16_t*>(e->vc[l]),
-        static_cast<int64_t>(c.max_slots) * D, c.max_slots);
-    RB_TRY(check_launch());
+    RB_TRY(launch_k(qkv_finish_kernel, gq, dim3(kQkvNT), 0, st, true, static_cast<const StepParams*>(e->d_params),
+                    static_cast<const int32_t*>(e->d_depths), static_cast<const float*>(e->part), s_qkv.splits, rows,
+                    H, HK, static_cast<const uint16_t*>(lw.q_norm), static_cast<const uint16_t*>(lw.k_norm),
+                    static_cast<const uint16_t*>(e->w.rope_cos), static_cast<const uint16_t*>(e->w.rope_sin),
+                    c.max_pos, c.rms_eps, e->qbuf, static_cast<uint16_t*>(e->kc[l]),
+                    static_cast<uint16_t*>(e->vc[l]), static_cast<int64_t>(c.max_slots) * D, c.max_slots));
     // attention over [prefix | committed | trie]
     AttnDev p{};
     p.H = H; p.M = rows; p.HK = HK; p.NP = 0; p.NN = 0;
@@ -402,32 +436,22 @@ int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
     RB_TRY(attn_launch_engine(p, e->apart, e->max_chunks, tq, e->m_kc[l], e->m_vc[l], st));
     // o projection + residual + post-attention norm
     g.epi = kEpiPartial;
-    RB_TRY(gemm_launch_maps(s_o, e->m_attn, e->m_o[l], g, st));
-    RB_TRY(launch_norm_nt(hid, [&](auto nt, auto ept) {
-      constexpr int NT = decltype(nt)::value, EPT = decltype(ept)::value;
-      resid_norm_kernel<NT, EPT><<<rows, NT, 0, st>>>(e->d_params, e->part, s_o.splits, rows, e->h,
-                                                 static_cast<const uint16_t*>(lw.post_norm), e->xn, hid, c.rms_eps);
-      return check_launch();
-    }));
+    RB_TRY(gemm_launch_maps(s_o, e->m_attn, e->m_o[l], g, st, true));
+    RB_TRY(launch_resid_norm(e, s_o.splits, rows, lw.post_norm, st));
     // gate|up with the SiLU*mul epilogue
     GemmLaunch gu{};
     gu.epi = kEpiSiluMul;
     gu.out = e->act;
     gu.ldo = c.ffn;
-    RB_TRY(gemm_launch_maps(s_gu, e->m_xn, e->m_gu[l], gu, st));
+    RB_TRY(gemm_launch_maps(s_gu, e->m_xn, e->m_gu[l], gu, st, true));
     // down + residual + next norm
     g.epi = kEpiPartial;
-    RB_TRY(gemm_launch_maps(s_d, e->m_act, e->m_d[l], g, st));
+    RB_TRY(gemm_launch_maps(s_d, e->m_act, e->m_d[l], g, st, true));
     const void* next_norm = (l + 1 < c.n_layers) ? e->layers[l + 1].in_norm : e->w.final_norm;
-    RB_TRY(launch_norm_nt(hid, [&](auto nt, auto ept) {
-      constexpr int NT = decltype(nt)::value, EPT = decltype(ept)::value;
-      resid_norm_kernel<NT, EPT><<<rows, NT, 0, st>>>(e->d_params, e->part, s_d.splits, rows, e->h,
-                                                 static_cast<const uint16_t*>(next_norm), e->xn, hid, c.rms_eps);
-      return check_launch();
-    }));
+    RB_TRY(launch_resid_norm(e, s_d.splits, rows, next_norm, st));
   }
-  // lm_head (fp32 scores) with the greedy choice (acceptance.py:11-23) folded in.
-  if (cudaMemsetAsync(e->keys, 0, static_cast<size_t>(rows) * 8, st) != cudaSuccess) return RB_ERR_CUDA;
+  // lm_head (fp32 scores) with the greedy choice (acceptance.py:11-23) folded in;
+  // the keys are zero on entry (zeroed at set-up, reset by the finalize kernel).
   GemmLaunch gl{};
   if (s_lm.splits == 1) {
     gl.epi = kEpiF32Argmax;
@@ -435,17 +459,18 @@ int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
     gl.ldo = c.vocab;
     gl.keys = e->keys;
     gl.excl = &e->d_params->act_off;
-    RB_TRY(gemm_launch_maps(s_lm, e->m_xn, e->m_lm, gl, st));
+    RB_TRY(gemm_launch_maps(s_lm, e->m_xn, e->m_lm, gl, st, true));
   } else {  // small vocabularies: split-K like rb_linear, fixed-order fp32 reduce
     gl.epi = kEpiPartial;
     gl.partial = e->part;
-    RB_TRY(gemm_launch_maps(s_lm, e->m_xn, e->m_lm, gl, st));
+    RB_TRY(gemm_launch_maps(s_lm, e->m_xn, e->m_lm, gl, st, true));
     RB_TRY(splitk_reduce(e->part, s_lm.splits, rows, c.vocab, e->logits, c.vocab, 1, st));
-    argmax_keys_kernel<<<dim3(8, rows), 256, 0, st>>>(e->d_params, e->logits, c.vocab, c.vocab, e->keys);
-    RB_TRY(check_launch());
+    RB_TRY(launch_k(argmax_keys_kernel, dim3(8, rows), dim3(256), 0, st, false,
+                    static_cast<const StepParams*>(e->d_params), static_cast<const float*>(e->logits),
+                    static_cast<int64_t>(c.vocab), c.vocab, e->keys));
   }
-  greedy_finalize_kernel<<<(rows + 127) / 128, 128, 0, st>>>(e->d_params, e->keys, e->d_out, rows);
-  return check_launch();
+  return launch_k(greedy_finalize_kernel, dim3((rows + 127) / 128), dim3(128), 0, st, true,
+                  static_cast<const StepParams*>(e->d_params), e->keys, e->d_out, rows);
 }
 
 int bucket_of(int q) {
@@ -534,6 +559,10 @@ int rb_engine_create(const rb_model_config* cfg, const rb_model_weights* w, void
   if (st != RB_OK) {
     delete e;
     return st != RB_ERR_INVALID_ARG ? RB_ERR_UNSUPPORTED : st;
+  }
+  if (cudaMemset(e->keys, 0, static_cast<size_t>(c.max_rows) * 8) != cudaSuccess) {
+    delete e;
+    return RB_ERR_CUDA;
   }
   e->pinned_bytes = sizeof(StepParams) + 3 * static_cast<size_t>(c.max_rows) * 4;
   if (cudaMallocHost(&e->pinned, e->pinned_bytes) != cudaSuccess ||

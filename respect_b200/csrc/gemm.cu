@@ -117,6 +117,7 @@ __global__ void __launch_bounds__(128, 1)
   const int kc0 = static_cast<int>(static_cast<int64_t>(split) * a.k_chunks / a.splits);
   const int kc1 = static_cast<int>(static_cast<int64_t>(split + 1) * a.k_chunks / a.splits);
   const int nk = kc1 - kc0;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmx);
@@ -139,9 +140,25 @@ __global__ void __launch_bounds__(128, 1)
 
   if (warp == 0 && lane == 0) {
     // TMA producer: one stage = MT token tiles + one weight tile, 64 K-elements.
+    // The weight tiles of the first stages do not depend on the previous
+    // kernel: they are requested before waiting for it (PDL), the token tiles
+    // after.
     const uint64_t pol_w = policy_evict_first();
     const uint64_t pol_x = policy_evict_last();
-    for (int i = 0; i < nk; ++i) {
+    const int npre = nk < C::kStages ? nk : C::kStages;
+    for (int i = 0; i < npre; ++i) {
+      mbar_arrive_expect_tx(full0 + 8 * i, C::kStageBytes);
+      tma_load_2d(smem_u32(smem + i * C::kStageBytes) + MT * kXTileBytes, &tmw, full0 + 8 * i, (kc0 + i) * kBK,
+                  n_tile * BN, pol_w);
+    }
+    pdl_wait();
+    for (int i = 0; i < npre; ++i) {
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+        tma_load_2d(smem_u32(smem + i * C::kStageBytes) + mt * kXTileBytes, &tmx, full0 + 8 * i, (kc0 + i) * kBK,
+                    (m_group * MT + mt) * kTileM, pol_x);
+    }
+    for (int i = npre; i < nk; ++i) {
       const int s = i % C::kStages;
       const uint32_t ph = (i / C::kStages) & 1;
       if (!mbar_wait(empty0 + 8 * s, ph ^ 1, 0x101)) break;
@@ -177,6 +194,7 @@ __global__ void __launch_bounds__(128, 1)
     if (ok) umma_commit(accum);
   }
   __syncwarp();
+  pdl_wait();  // outputs are written after the previous kernel has completed
 
   // Epilogue: warp w owns TMEM lanes [32w, 32w+32) = token rows of each tile.
   // tcgen05.ld is warp-collective: the whole warp takes the same branch.
@@ -282,31 +300,30 @@ int gemm_encode_w(CUtensorMap* m, const void* w, int N, int K, int64_t ldw, int 
 
 template <int BN, int MT, int EPI>
 static int launch_t(const GemmShape& s, const CUtensorMap& mx, const CUtensorMap& mw,
-                    const GemmKernelArgs& ka, cudaStream_t stream) {
+                    const GemmKernelArgs& ka, cudaStream_t stream, bool pdl) {
   using C = GemmCfg<BN, MT>;
   auto kern = gemm_kernel<BN, MT, EPI>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
     return RB_ERR_CUDA;
   dim3 grid(s.n_tiles, s.splits, s.m_groups);
-  kern<<<grid, 128, C::kSmemBytes, stream>>>(mx, mw, ka);
-  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;
+  return launch_k(kern, grid, dim3(128), C::kSmemBytes, stream, pdl, mx, mw, ka);
 }
 
 template <int BN, int MT>
 static int launch_epi(const GemmShape& s, const CUtensorMap& mx, const CUtensorMap& mw,
-                      const GemmKernelArgs& ka, int epi, cudaStream_t stream) {
+                      const GemmKernelArgs& ka, int epi, cudaStream_t stream, bool pdl) {
   switch (epi) {
-    case kEpiStoreBF16: return launch_t<BN, MT, kEpiStoreBF16>(s, mx, mw, ka, stream);
-    case kEpiStoreF32: return launch_t<BN, MT, kEpiStoreF32>(s, mx, mw, ka, stream);
-    case kEpiSiluMul: return launch_t<BN, MT, kEpiSiluMul>(s, mx, mw, ka, stream);
-    case kEpiPartial: return launch_t<BN, MT, kEpiPartial>(s, mx, mw, ka, stream);
-    case kEpiF32Argmax: return launch_t<BN, MT, kEpiF32Argmax>(s, mx, mw, ka, stream);
+    case kEpiStoreBF16: return launch_t<BN, MT, kEpiStoreBF16>(s, mx, mw, ka, stream, pdl);
+    case kEpiStoreF32: return launch_t<BN, MT, kEpiStoreF32>(s, mx, mw, ka, stream, pdl);
+    case kEpiSiluMul: return launch_t<BN, MT, kEpiSiluMul>(s, mx, mw, ka, stream, pdl);
+    case kEpiPartial: return launch_t<BN, MT, kEpiPartial>(s, mx, mw, ka, stream, pdl);
+    case kEpiF32Argmax: return launch_t<BN, MT, kEpiF32Argmax>(s, mx, mw, ka, stream, pdl);
   }
   return RB_ERR_INVALID_ARG;
 }
 
 int gemm_launch_maps(const GemmShape& s, const CUtensorMap& mx, const CUtensorMap& mw,
-                     const GemmLaunch& a, cudaStream_t stream) {
+                     const GemmLaunch& a, cudaStream_t stream, bool pdl) {
   GemmKernelArgs ka{};
   ka.M = s.M; ka.N = s.N; ka.K = s.K;
   ka.k_chunks = s.k_chunks;
@@ -322,12 +339,12 @@ int gemm_launch_maps(const GemmShape& s, const CUtensorMap& mx, const CUtensorMa
   if (a.epi == kEpiSiluMul && (s.N % s.BN) != 0) return RB_ERR_UNSUPPORTED;
   const int key = s.BN * 4 + s.mt;
   switch (key) {
-    case 256 * 4 + 1: return launch_epi<256, 1>(s, mx, mw, ka, a.epi, stream);
-    case 256 * 4 + 2: return launch_epi<256, 2>(s, mx, mw, ka, a.epi, stream);
-    case 208 * 4 + 1: return launch_epi<208, 1>(s, mx, mw, ka, a.epi, stream);
-    case 208 * 4 + 2: return launch_epi<208, 2>(s, mx, mw, ka, a.epi, stream);
-    case 128 * 4 + 1: return launch_epi<128, 1>(s, mx, mw, ka, a.epi, stream);
-    case 128 * 4 + 2: return launch_epi<128, 2>(s, mx, mw, ka, a.epi, stream);
+    case 256 * 4 + 1: return launch_epi<256, 1>(s, mx, mw, ka, a.epi, stream, pdl);
+    case 256 * 4 + 2: return launch_epi<256, 2>(s, mx, mw, ka, a.epi, stream, pdl);
+    case 208 * 4 + 1: return launch_epi<208, 1>(s, mx, mw, ka, a.epi, stream, pdl);
+    case 208 * 4 + 2: return launch_epi<208, 2>(s, mx, mw, ka, a.epi, stream, pdl);
+    case 128 * 4 + 1: return launch_epi<128, 1>(s, mx, mw, ka, a.epi, stream, pdl);
+    case 128 * 4 + 2: return launch_epi<128, 2>(s, mx, mw, ka, a.epi, stream, pdl);
   }
   return RB_ERR_UNSUPPORTED;
 }
@@ -338,7 +355,7 @@ int gemm_launch(const GemmShape& s, const GemmLaunch& a, cudaStream_t stream) {
   if (st != RB_OK) return st;
   st = gemm_encode_w(&mw, a.w, s.N, s.K, a.ldw, s.BN);
   if (st != RB_OK) return st;
-  return gemm_launch_maps(s, mx, mw, a, stream);
+  return gemm_launch_maps(s, mx, mw, a, stream, false);
 }
 
 // ------------------------------------------------------------ split-K reduce

@@ -71,8 +71,10 @@ struct GemmLaunch {
 int gemm_launch(const GemmShape& s, const GemmLaunch& a, cudaStream_t stream);
 
 // Same, with pre-encoded tensor maps (engine path: encoded once at set-up).
+// pdl: launch with programmatic stream serialization (weight prefetch overlaps
+// the previous kernel; see pdl_wait in common.cuh).
 int gemm_launch_maps(const GemmShape& s, const CUtensorMap& mx, const CUtensorMap& mw,
-                     const GemmLaunch& a, cudaStream_t stream);
+                     const GemmLaunch& a, cudaStream_t stream, bool pdl = false);
 int gemm_encode_x(CUtensorMap* m, const void* x, int M, int K, int64_t ldx);
 int gemm_encode_w(CUtensorMap* m, const void* w, int N, int K, int64_t ldw, int BN);
 
