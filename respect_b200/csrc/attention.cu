@@ -139,66 +139,99 @@ __device__ __forceinline__ bool node_allowed(const AttnDev& p, int row, int j) {
   }
 }
 
-// Fold up to 8 node slots into (m, l, acc), in the order given. Scores are
-// computed for the whole batch first (the 8 warp trees interleave), then the
-// online-softmax updates run one slot at a time:
-//   s = (q.k) by a fixed warp tree, lane 0's sum broadcast, times scale*log2(e)
+// Node phase. A row's allowed node slots are visited in slot order, in
+// batches of up to 32: lane u scores the batch's u-th slot (q.k over the 128
+// dims in ascending order, fp32, times scale*log2(e)), then the batch is folded
+// one slot at a time:
 //   m' = max(m, s); a = 2^(m - m'); p = 2^(s - m'); acc = p*v + acc*a; l = l*a + p
-// Every slot goes through exactly this arithmetic whatever the masking mode or
-// batch boundaries, so a row's bits depend only on its allowed slots' order.
-constexpr int kNodeBatch = 8;
+// (lane u of the fold owns dims [4u, 4u+4)). Every slot goes through exactly
+// this arithmetic whatever the masking mode or batch boundaries, so a row's
+// bits depend only on its allowed slots and their order.
+constexpr int kMaxTrieDepth = 1024;
+constexpr int kChunkGroup = 4;  // chunk partials loaded together
+constexpr int kVPrefetch = 16;
 
 template <typename T>
-__device__ __forceinline__ void fold_batch(const AttnDev& p, const T* kn, const T* vn, int kvh,
-                                           const int (&slot)[kNodeBatch], int cnt, const float (&qv)[4], int d0,
-                                           float scale2, float& m, float& l, float (&acc)[4]) {
-  float kv[kNodeBatch][4], vv[kNodeBatch][4], s[kNodeBatch];
+__device__ __forceinline__ float dot128(const T* krow, const float* qs);
+template <>
+__device__ __forceinline__ float dot128<uint16_t>(const uint16_t* krow, const float* qs) {
+  float s = 0.f;
 #pragma unroll
-  for (int u = 0; u < kNodeBatch; ++u) {
-    if (u < cnt) {
-      ld4(kn + kvh * p.sknh + static_cast<int64_t>(slot[u]) * p.sknn + d0, kv[u]);
-      ld4(vn + kvh * p.svnh + static_cast<int64_t>(slot[u]) * p.svnn + d0, vv[u]);
-    } else {
+  for (int c = 0; c < 16; ++c) {
+    const uint4 k8 = reinterpret_cast<const uint4*>(krow)[c];
+    const float4 qa = reinterpret_cast<const float4*>(qs)[2 * c];
+    const float4 qb = reinterpret_cast<const float4*>(qs)[2 * c + 1];
+    s = fmaf(qa.x, bf16_bits_to_f32(static_cast<uint16_t>(k8.x)), s);
+    s = fmaf(qa.y, bf16_bits_to_f32(static_cast<uint16_t>(k8.x >> 16)), s);
+    s = fmaf(qa.z, bf16_bits_to_f32(static_cast<uint16_t>(k8.y)), s);
+    s = fmaf(qa.w, bf16_bits_to_f32(static_cast<uint16_t>(k8.y >> 16)), s);
+    s = fmaf(qb.x, bf16_bits_to_f32(static_cast<uint16_t>(k8.z)), s);
+    s = fmaf(qb.y, bf16_bits_to_f32(static_cast<uint16_t>(k8.z >> 16)), s);
+    s = fmaf(qb.z, bf16_bits_to_f32(static_cast<uint16_t>(k8.w)), s);
+    s = fmaf(qb.w, bf16_bits_to_f32(static_cast<uint16_t>(k8.w >> 16)), s);
+  }
+  return s;
+}
+template <>
+__device__ __forceinline__ float dot128<float>(const float* krow, const float* qs) {
+  float s = 0.f;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) kv[u][e] = vv[u][e] = 0.f;
+  for (int c = 0; c < 32; ++c) {
+    const float4 k4 = reinterpret_cast<const float4*>(krow)[c];
+    const float4 q4 = reinterpret_cast<const float4*>(qs)[c];
+    s = fmaf(q4.x, k4.x, s);
+    s = fmaf(q4.y, k4.y, s);
+    s = fmaf(q4.z, k4.z, s);
+    s = fmaf(q4.w, k4.w, s);
+  }
+  return s;
+}
+
+// Fold the batch: `valid` marks lanes holding a slot (folded in lane order).
+template <typename T>
+__device__ __forceinline__ void fold_lanes(const AttnDev& p, const T* kn, const T* vn, int kvh, int lane,
+                                           unsigned valid, int slot, const float* qs, int d0, float scale2,
+                                           float& m, float& l, float (&acc)[4]) {
+  float sc = 0.f;
+  if ((valid >> lane) & 1u) sc = dot128<T>(kn + kvh * p.sknh + static_cast<int64_t>(slot) * p.sknn, qs) * scale2;
+  while (valid) {
+    // prefetch the value rows of the next (up to) kVPrefetch slots
+    float vv[kVPrefetch][4];
+    int us[kVPrefetch];
+    int cnt = 0;
+#pragma unroll
+    for (int u = 0; u < kVPrefetch; ++u) {
+      us[u] = valid ? __ffs(valid) - 1 : 0;
+      if (valid) {
+        valid &= valid - 1;
+        ++cnt;
+      }
+      const int su = __shfl_sync(0xffffffffu, slot, us[u]);
+      if (u < cnt) ld4(vn + kvh * p.svnh + static_cast<int64_t>(su) * p.svnn + d0, vv[u]);
     }
-  }
 #pragma unroll
-  for (int u = 0; u < kNodeBatch; ++u) {
-    float t = qv[0] * kv[u][0];
-    t = fmaf(qv[1], kv[u][1], t);
-    t = fmaf(qv[2], kv[u][2], t);
-    t = fmaf(qv[3], kv[u][3], t);
-    s[u] = t;
-  }
+    for (int u = 0; u < kVPrefetch; ++u) {
+      const float su = __shfl_sync(0xffffffffu, sc, us[u]);
+      if (u < cnt) {
+        const float m_new = fmaxf(m, su);
+        const float a = fast_exp2(m - m_new);
+        const float pe = fast_exp2(su - m_new);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-    for (int u = 0; u < kNodeBatch; ++u) s[u] += __shfl_xor_sync(0xffffffffu, s[u], o);
-  }
-#pragma unroll
-  for (int u = 0; u < kNodeBatch; ++u) {
-    if (u < cnt) {
-      const float su = __shfl_sync(0xffffffffu, s[u], 0) * scale2;
-      const float m_new = fmaxf(m, su);
-      const float a = fast_exp2(m - m_new);
-      const float pe = fast_exp2(su - m_new);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[e] = fmaf(pe, vv[u][e], acc[e] * a);
-      l = fmaf(l, a, pe);
-      m = m_new;
+        for (int e = 0; e < 4; ++e) acc[e] = fmaf(pe, vv[u][e], acc[e] * a);
+        l = fmaf(l, a, pe);
+        m = m_new;
+      }
     }
   }
 }
 
-constexpr int kMaxTrieDepth = 1024;
-
-// One warp per (head, query row); lane owns dims [4*lane, 4*lane+4).
+// One warp per (head, query row); lane owns dims [4*lane, 4*lane+4) of the output.
 template <typename T>
 __global__ void __launch_bounds__(128) attn_nodes(const AttnDev p, const float* __restrict__ part) {
   constexpr int D = 128;
   __shared__ int chain[4][kMaxTrieDepth];
   __shared__ int par_s[kMaxTrieDepth];
+  __shared__ __align__(16) float qs[4][D];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 4 + warp;
   const int h = blockIdx.y;
@@ -232,26 +265,40 @@ __global__ void __launch_bounds__(128) attn_nodes(const AttnDev p, const float* 
   const T* vn = p.vn ? static_cast<const T*>(p.vn) : static_cast<const T*>(p.vp) + static_cast<int64_t>(NP) * p.svpn;
   float qv[4];
   ld4(q + h * p.sqh + static_cast<int64_t>(row) * p.sqm + d0, qv);
+  *reinterpret_cast<float4*>(&qs[warp][d0]) = make_float4(qv[0], qv[1], qv[2], qv[3]);
 
-  // Merge prefix chunks in ascending chunk order.
+  // Prefix chunk partials, merged in ascending chunk order (loads of a group
+  // of chunks issued together).
   float m = -INFINITY, l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int c = 0; c < nchunks; ++c) {
-    const float* o = part + ((static_cast<int64_t>(c) * p.H + h) * p.M + row) * kPartStride;
-    const float mc = o[D];
-    if (mc == -INFINITY) continue;
-    const float lc = o[D + 1];
-    const float4 ac = *reinterpret_cast<const float4*>(o + d0);
-    const float m_new = fmaxf(m, mc);
-    const float a = fast_exp2(m - m_new);
-    const float b = fast_exp2(mc - m_new);
-    acc[0] = fmaf(ac.x, b, acc[0] * a); acc[1] = fmaf(ac.y, b, acc[1] * a);
-    acc[2] = fmaf(ac.z, b, acc[2] * a); acc[3] = fmaf(ac.w, b, acc[3] * a);
-    l = fmaf(lc, b, l * a);
-    m = m_new;
+  for (int c0 = 0; c0 < nchunks; c0 += kChunkGroup) {
+    float cm[kChunkGroup], cl[kChunkGroup];
+    float4 ca[kChunkGroup];
+#pragma unroll
+    for (int g = 0; g < kChunkGroup; ++g) {
+      cm[g] = -INFINITY;
+      if (c0 + g < nchunks) {
+        const float* o = part + ((static_cast<int64_t>(c0 + g) * p.H + h) * p.M + row) * kPartStride;
+        cm[g] = o[D];
+        cl[g] = o[D + 1];
+        ca[g] = *reinterpret_cast<const float4*>(o + d0);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < kChunkGroup; ++g) {
+      if (cm[g] != -INFINITY) {
+        const float m_new = fmaxf(m, cm[g]);
+        const float a = fast_exp2(m - m_new);
+        const float b = fast_exp2(cm[g] - m_new);
+        acc[0] = fmaf(ca[g].x, b, acc[0] * a); acc[1] = fmaf(ca[g].y, b, acc[1] * a);
+        acc[2] = fmaf(ca[g].z, b, acc[2] * a); acc[3] = fmaf(ca[g].w, b, acc[3] * a);
+        l = fmaf(cl[g], b, l * a);
+        m = m_new;
+      }
+    }
   }
+  __syncwarp();  // qs of this warp written
 
   const float scale2 = p.sm_scale * kLog2e;
-  int slot[kNodeBatch];
   if (p.mask_kind == kMaskTrie) {
     // Committed slots, in order, then the ancestors-or-self of this node in
     // increasing index (= slot) order; every other slot is masked.
@@ -277,32 +324,19 @@ __global__ void __launch_bounds__(128) attn_nodes(const AttnDev p, const float* 
     depth = __shfl_sync(0xffffffffu, depth, 0);
     __syncwarp();
     const int total = base + depth + 1;
-    for (int b0 = 0; b0 < total; b0 += kNodeBatch) {
-      const int cnt = min(kNodeBatch, total - b0);
-#pragma unroll
-      for (int u = 0; u < kNodeBatch; ++u) {
-        const int i = b0 + u;
-        slot[u] = i < base ? i : (i < total ? base + chain[warp][i - base] : 0);
-      }
-      fold_batch<T>(p, kn, vn, kvh, slot, cnt, qv, d0, scale2, m, l, acc);
+    for (int b0 = 0; b0 < total; b0 += 32) {
+      const int i = b0 + lane;
+      const int slot = i < base ? i : (i < total ? base + chain[warp][i - base] : 0);
+      const unsigned valid = __ballot_sync(0xffffffffu, i < total);
+      fold_lanes<T>(p, kn, vn, kvh, lane, valid, slot, qs[warp], d0, scale2, m, l, acc);
     }
   } else {
     // Node slots in slot order, allowed ones only (a masked slot is an exact no-op).
-    int cnt = 0;
     for (int j0 = 0; j0 < p.NN; j0 += 32) {
       const int j = j0 + lane;
-      const bool allow = j < p.NN && node_allowed(p, row, j);
-      unsigned bits = __ballot_sync(0xffffffffu, allow);
-      while (bits) {
-        slot[cnt++] = j0 + __ffs(bits) - 1;
-        bits &= bits - 1;
-        if (cnt == kNodeBatch) {
-          fold_batch<T>(p, kn, vn, kvh, slot, cnt, qv, d0, scale2, m, l, acc);
-          cnt = 0;
-        }
-      }
+      const unsigned valid = __ballot_sync(0xffffffffu, j < p.NN && node_allowed(p, row, j));
+      if (valid) fold_lanes<T>(p, kn, vn, kvh, lane, valid, j, qs[warp], d0, scale2, m, l, acc);
     }
-    if (cnt) fold_batch<T>(p, kn, vn, kvh, slot, cnt, qv, d0, scale2, m, l, acc);
   }
 #pragma unroll
   for (int e = 0; e < 4; ++e) {

@@ -5,8 +5,10 @@
 //
 //   S = Q K^T            tcgen05.mma, M=128 rows, N=128 keys, K=128 dims -> TMEM
 //   m' = max(m, rowmax(S*scale)); alpha = 2^(m - m'); p = 2^(S*scale - m')
-//   O = bf16(p) V        tcgen05.mma, A = P (smem, K-major), B = V (MN-major)
-//   acc = acc*alpha + O; l = l*alpha + sum(p)     (fp32, one row per thread)
+//   O = O*alpha (in TMEM, by the softmax threads); l = l*alpha + sum(p)
+//   O += bf16(p) V       tcgen05.mma, A = P (smem, K-major), B = V (MN-major)
+// The output accumulator never leaves TMEM until the chunk is done, so the
+// softmax of tile j+1 runs while the tensor core computes P_j V_j.
 //
 // Warp roles: warps 0-7 softmax / correction (two threads per query row: warp
 // w serves TMEM lanes 32*(w%4).., key / dim columns [64*(w/4), 64*(w/4)+64);
@@ -36,7 +38,7 @@ constexpr int kSoftmaxThreads = 256;
 constexpr int kThreads = kSoftmaxThreads + 64;
 constexpr int kProducerWarp = 8, kMmaWarp = 9;
 // barrier indices
-enum { Q_FULL = 0, KV_FULL = 1, KV_EMPTY = 3, S_FULL = 5, P_FULL = 7, O_FULL = 8, O_FREE = 9, NBAR = 10 };
+enum { Q_FULL = 0, KV_FULL = 1, KV_EMPTY = 3, S_FULL = 5, P_FULL = 7, O_FULL = 8, NBAR = 9 };
 constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, 0, 0);
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, 0, 1);
 }  // namespace tc
@@ -75,7 +77,6 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     mbar_init(bar(S_FULL + 1), 1);
     mbar_init(bar(P_FULL), kSoftmaxThreads);
     mbar_init(bar(O_FULL), 1);
-    mbar_init(bar(O_FREE), kSoftmaxThreads);
     fence_mbar_init();
   }
   if (warp == kMmaWarp) {
@@ -130,15 +131,15 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           tc_fence_after();
           issue_qk(j + 1);
         }
+        // P_j written and O rescaled by alpha_j (both signalled by P_FULL)
         if (!mbar_wait(bar(P_FULL), j & 1, 0x215)) break;
-        if (j > 0 && !mbar_wait(bar(O_FREE), (j - 1) & 1, 0x216)) break;
         tc_fence_after();
         const uint32_t sv = sKV + (j & 1) * kStage + 2 * kHalf;
 #pragma unroll
         for (int kk = 0; kk < kKeys / 16; ++kk) {
           const uint32_t pa = sP + (kk >> 2) * kHalf + (kk & 3) * 32;
           umma_bf16(tmem + 256, sdesc_kmajor_sw128(pa), sdesc_mnmajor_sw128(sv + kk * 2048, kHalf), kIdescPV,
-                    kk ? 1u : 0u);
+                    (j | kk) ? 1u : 0u);
         }
         umma_commit(bar(O_FULL));
         if (j + 2 < ntiles) umma_commit(bar(KV_EMPTY + (j & 1)));
@@ -153,20 +154,25 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     float* red = reinterpret_cast<float*>(smem + kRedOff);  // [2 (max|sum)][2 (half)][128] floats
     const float scale2 = p.sm_scale * 1.4426950408889634f;
     float m = -INFINITY, l = 0.f;
-    float acc[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+    // A timed-out wait (device error already raised) skips this warp's TMEM
+    // work but never a named barrier, so the other warps cannot block.
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(bar(S_FULL + (j & 1)), (j >> 1) & 1, 0x217));
-      if (!ok) break;
-      tc_fence_after();
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(S_FULL + (j & 1)), (j >> 1) & 1, 0x217));
       const uint32_t sb = lane_base + (j & 1) * 128 + hf * 64;
       const int nvalid = min(kKeys, k1 - (k0 + j * kKeys)) - hf * 64;  // valid keys in this half (may be <= 0)
       uint32_t raw[4][16];
+      if (ok) {
+        tc_fence_after();
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) tmem_ld16_nowait(sb + cc * 16, raw[cc]);
-      tmem_wait_ld();
+        for (int cc = 0; cc < 4; ++cc) tmem_ld16_nowait(sb + cc * 16, raw[cc]);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+          for (int i = 0; i < 16; ++i) raw[cc][i] = 0u;
+      }
       float sv[64];
       float mx = -INFINITY;
 #pragma unroll
@@ -180,37 +186,59 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       const float m_new = fmaxf(m, mx);  // finite: every tile has a valid key in its lower half
       const float alpha = fast_exp2(m - m_new);
       float rs = 0.f;
-      uint8_t* rowp = smem + kPOff + hf * kHalf + r * 128;
+      uint32_t w[32];
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {  // 8 keys = one 16-byte chunk of the swizzled row
-        uint32_t w[4];
-#pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-          const float p0 = fast_exp2(sv[cc * 8 + i] - m_new);
-          const float p1 = fast_exp2(sv[cc * 8 + i + 1] - m_new);
-          rs += p0;
-          rs += p1;
-          w[i / 2] = pack_bf16x2(p0, p1);
-        }
-        *reinterpret_cast<uint4*>(rowp + ((cc ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      for (int i = 0; i < 64; i += 2) {
+        const float p0 = fast_exp2(sv[i] - m_new);
+        const float p1 = fast_exp2(sv[i + 1] - m_new);
+        rs += p0;
+        rs += p1;
+        w[i / 2] = pack_bf16x2(p0, p1);
       }
       red[256 + hf * 128 + r] = rs;
+      if (j > 0 && ok) {
+        // P_{j-1} V_{j-1} must be complete before P_j overwrites P and O is rescaled.
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(O_FULL), (j - 1) & 1, 0x218));
+        if (ok) {
+          tc_fence_after();
+          const uint32_t ob = lane_base + 256 + hf * 64;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) tmem_ld16_nowait(ob + cc * 16, raw[cc]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) raw[cc][i] = __float_as_uint(__uint_as_float(raw[cc][i]) * alpha);
+            tmem_st16(ob + cc * 16, raw[cc]);
+          }
+          tmem_wait_st();
+        }
+      }
+      if (ok) {
+        uint8_t* rowp = smem + kPOff + hf * kHalf + r * 128;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc)  // 8 keys = one 16-byte chunk of the swizzled row
+          *reinterpret_cast<uint4*>(rowp + ((cc ^ (r & 7)) << 4)) =
+              make_uint4(w[cc * 4], w[cc * 4 + 1], w[cc * 4 + 2], w[cc * 4 + 3]);
+      }
       fence_proxy_async_smem();  // P stores -> visible to the tensor core (async proxy)
-      tc_fence_before();         // S loads of this tile ordered before the arrive
+      tc_fence_before();         // S loads and O stores of this tile ordered before the arrive
       mbar_arrive(bar(P_FULL));
       named_bar(1, kSoftmaxThreads);
       l = fmaf(l, alpha, red[256 + r] + red[384 + r]);
-      ok = __all_sync(0xffffffffu, mbar_wait(bar(O_FULL), j & 1, 0x218));
-      if (!ok) break;
+      m = m_new;
+    }
+    // the last P V product, then O leaves TMEM once
+    float acc[64];
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(O_FULL), (ntiles - 1) & 1, 0x219));
+    if (ok) {
       tc_fence_after();
+      uint32_t raw[4][16];
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) tmem_ld16_nowait(lane_base + 256 + hf * 64 + cc * 16, raw[cc]);
       tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < 64; ++i) acc[i] = fmaf(acc[i], alpha, __uint_as_float(raw[i >> 4][i & 15]));
-      tc_fence_before();
-      mbar_arrive(bar(O_FREE));
-      m = m_new;
+      for (int i = 0; i < 64; ++i) acc[i] = __uint_as_float(raw[i >> 4][i & 15]);
     }
     const int row = rt * kRows + r;
     if (ok && row < M) {
