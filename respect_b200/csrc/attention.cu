@@ -1,7 +1,7 @@
 // Deterministic trie-verification attention (respect/kernels/attention.py:15-96).
 //
 // Phase 1 (prefix, keys [0, NP)): the prefix is cut into chunks of
-// kPrefixChunk keys at ABSOLUTE positions (chunk c = [c*C, (c+1)*C)), each
+// C = prefix_chunk(NP, H) keys at ABSOLUTE positions (chunk c = [c*C, (c+1)*C)), each
 // chunk reduced by an online softmax over fixed key tiles into a partial
 // (max, sum, acc[D]) per query row. Chunk boundaries depend on NP only.
 // Phase 2 (per query row, one warp): merge the chunk partials in chunk order,
@@ -53,8 +53,9 @@ __global__ void __launch_bounds__(128) attn_prefix_simt(const AttnDev p, float* 
   pdl_wait();
   const int NP = p.sp ? p.sp->prompt_len : p.NP;
   const int M = p.sp ? min(p.M, p.sp->q) : p.M;
-  const int k0 = c * kPrefixChunk;
-  const int k1 = min(NP, k0 + kPrefixChunk);
+  const int C = prefix_chunk(NP, p.H);
+  const int k0 = c * C;
+  const int k1 = min(NP, k0 + C);
   if (k0 >= k1 || r0 >= M) return;  // chunk beyond the prefix / rows beyond the live ones
   const T* q = static_cast<const T*>(p.q);
   const T* kp = static_cast<const T*>(p.kp);
@@ -140,21 +141,32 @@ __device__ __forceinline__ bool node_allowed(const AttnDev& p, int row, int j) {
 }
 
 // Node phase. A row's allowed node slots are visited in slot order, in
-// batches of up to 32: lane u scores the batch's u-th slot (q.k over the 128
+// batches of up to 32. Lane u scores the batch's u-th slot (q.k over the 128
 // dims in ascending order, fp32, times scale*log2(e)), then the batch is folded
 // one slot at a time:
 //   m' = max(m, s); a = 2^(m - m'); p = 2^(s - m'); acc = p*v + acc*a; l = l*a + p
 // (lane u of the fold owns dims [4u, 4u+4)). Every slot goes through exactly
 // this arithmetic whatever the masking mode or batch boundaries, so a row's
 // bits depend only on its allowed slots and their order.
+//
+// One block = one query row x one kv head; warp g serves query head
+// kvh*G + g (G = H / HK). The row's slots (committed, then trie ancestors, or
+// the allowed mask entries) are the same for all G heads, so each batch of
+// node K / V rows is staged in shared memory once for the whole group.
 constexpr int kMaxTrieDepth = 1024;
 constexpr int kChunkGroup = 4;  // chunk partials loaded together
-constexpr int kVPrefetch = 16;
+constexpr int kMaxGroup = 16;   // query heads per kv head handled by one block
 
 template <typename T>
-__device__ __forceinline__ float dot128(const T* krow, const float* qs);
+struct NodeSmem {
+  static constexpr int kRow = 128 * static_cast<int>(sizeof(T));  // bytes of one K / V row
+  static constexpr int kKPitch = kRow + 16;                         // padded: conflict-free lane-per-row reads
+};
+
+template <typename T>
+__device__ __forceinline__ float dot128_smem(const uint8_t* krow, const float* qs);
 template <>
-__device__ __forceinline__ float dot128<uint16_t>(const uint16_t* krow, const float* qs) {
+__device__ __forceinline__ float dot128_smem<uint16_t>(const uint8_t* krow, const float* qs) {
   float s = 0.f;
 #pragma unroll
   for (int c = 0; c < 16; ++c) {
@@ -173,7 +185,7 @@ __device__ __forceinline__ float dot128<uint16_t>(const uint16_t* krow, const fl
   return s;
 }
 template <>
-__device__ __forceinline__ float dot128<float>(const float* krow, const float* qs) {
+__device__ __forceinline__ float dot128_smem<float>(const uint8_t* krow, const float* qs) {
   float s = 0.f;
 #pragma unroll
   for (int c = 0; c < 32; ++c) {
@@ -187,63 +199,23 @@ __device__ __forceinline__ float dot128<float>(const float* krow, const float* q
   return s;
 }
 
-// Fold the batch: `valid` marks lanes holding a slot (folded in lane order).
 template <typename T>
-__device__ __forceinline__ void fold_lanes(const AttnDev& p, const T* kn, const T* vn, int kvh, int lane,
-                                           unsigned valid, int slot, const float* qs, int d0, float scale2,
-                                           float& m, float& l, float (&acc)[4]) {
-  float sc = 0.f;
-  if ((valid >> lane) & 1u) sc = dot128<T>(kn + kvh * p.sknh + static_cast<int64_t>(slot) * p.sknn, qs) * scale2;
-  while (valid) {
-    // prefetch the value rows of the next (up to) kVPrefetch slots
-    float vv[kVPrefetch][4];
-    int us[kVPrefetch];
-    int cnt = 0;
-#pragma unroll
-    for (int u = 0; u < kVPrefetch; ++u) {
-      us[u] = valid ? __ffs(valid) - 1 : 0;
-      if (valid) {
-        valid &= valid - 1;
-        ++cnt;
-      }
-      const int su = __shfl_sync(0xffffffffu, slot, us[u]);
-      if (u < cnt) ld4(vn + kvh * p.svnh + static_cast<int64_t>(su) * p.svnn + d0, vv[u]);
-    }
-#pragma unroll
-    for (int u = 0; u < kVPrefetch; ++u) {
-      const float su = __shfl_sync(0xffffffffu, sc, us[u]);
-      if (u < cnt) {
-        const float m_new = fmaxf(m, su);
-        const float a = fast_exp2(m - m_new);
-        const float pe = fast_exp2(su - m_new);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] = fmaf(pe, vv[u][e], acc[e] * a);
-        l = fmaf(l, a, pe);
-        m = m_new;
-      }
-    }
-  }
-}
-
-// One warp per (head, query row); lane owns dims [4*lane, 4*lane+4) of the output.
-template <typename T>
-__global__ void __launch_bounds__(128) attn_nodes(const AttnDev p, const float* __restrict__ part) {
+__global__ void __launch_bounds__(32 * kMaxGroup) attn_nodes(const AttnDev p, const float* __restrict__ part) {
   constexpr int D = 128;
-  __shared__ int chain[4][kMaxTrieDepth];
-  __shared__ int par_s[kMaxTrieDepth];
-  __shared__ __align__(16) float qs[4][D];
+  using L = NodeSmem<T>;
+  __shared__ int chain[kMaxTrieDepth];
+  __shared__ int slots[32];
+  __shared__ int nslots;
+  __shared__ __align__(16) float qs[kMaxGroup][D];
+  __shared__ __align__(16) uint8_t ks[32][L::kKPitch];
+  __shared__ __align__(16) uint8_t vs[32][L::kRow];
+  const int G = p.H / p.HK;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 4 + warp;
-  const int h = blockIdx.y;
+  const int row = blockIdx.x, kvh = blockIdx.y;
+  const int h = kvh * G + warp;
+  const int nthr = G * 32;
   pdl_trigger();
   pdl_wait();
-  if (p.mask_kind == kMaskTrie) {
-    // the block's rows walk their parent chains in shared memory
-    const int nq = min(p.sp ? p.sp->q : p.M, kMaxTrieDepth);
-    for (int i = threadIdx.x; i < nq; i += blockDim.x) par_s[i] = p.parents[i];
-    __syncthreads();
-  }
-  if (row >= p.M) return;
   const int d0 = lane * 4;
   T* out = static_cast<T*>(p.out) + h * p.soh + static_cast<int64_t>(row) * p.som + d0;
   const int live = p.sp ? p.sp->q : p.M;
@@ -256,19 +228,45 @@ __global__ void __launch_bounds__(128) attn_nodes(const AttnDev p, const float* 
     return;
   }
   const int NP = p.sp ? p.sp->prompt_len : p.NP;
-  const int nchunks = (NP + kPrefixChunk - 1) / kPrefixChunk;
-  const int kvh = h / (p.H / p.HK);
-  const T* q = static_cast<const T*>(p.q);
+  const int nchunks = prefix_nchunks(NP, p.H);
   // Node slot 0 sits right after the prefix; without explicit node tensors
   // (engine path) the node segment is the same buffer from key NP on.
   const T* kn = p.kn ? static_cast<const T*>(p.kn) : static_cast<const T*>(p.kp) + static_cast<int64_t>(NP) * p.skpn;
   const T* vn = p.vn ? static_cast<const T*>(p.vn) : static_cast<const T*>(p.vp) + static_cast<int64_t>(NP) * p.svpn;
+  const int64_t kbase = static_cast<int64_t>(kvh) * p.sknh, vbase = static_cast<int64_t>(kvh) * p.svnh;
+
+  // Trie mode: the row's ancestor chain (root first), walked once by thread 0.
+  int base = 0, depth = -1;
+  if (p.mask_kind == kMaskTrie) {
+    base = p.sp ? p.sp->base : p.causal_first;
+    if (threadIdx.x == 0) {
+      int dd = p.depths[row];
+      if (dd < 0 || dd >= kMaxTrieDepth || dd > row) {
+        raise_device_error(0x201);
+        dd = -1;
+      }
+      int a = row;
+      for (int t = dd; t >= 0; --t) {
+        chain[t] = a;
+        const int par = p.parents[a];
+        if ((t > 0 && (par < 0 || par >= a)) || (t == 0 && par != -1)) {
+          raise_device_error(0x202);  // parents / depths inconsistent: fold nothing more
+          dd = -1;
+          break;
+        }
+        a = par;
+      }
+      nslots = dd;  // reuse as a broadcast of the depth
+    }
+    __syncthreads();
+    depth = nslots;
+  }
+
   float qv[4];
-  ld4(q + h * p.sqh + static_cast<int64_t>(row) * p.sqm + d0, qv);
+  ld4(static_cast<const T*>(p.q) + h * p.sqh + static_cast<int64_t>(row) * p.sqm + d0, qv);
   *reinterpret_cast<float4*>(&qs[warp][d0]) = make_float4(qv[0], qv[1], qv[2], qv[3]);
 
-  // Prefix chunk partials, merged in ascending chunk order (loads of a group
-  // of chunks issued together).
+  // Prefix chunk partials, merged in ascending chunk order.
   float m = -INFINITY, l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int c0 = 0; c0 < nchunks; c0 += kChunkGroup) {
     float cm[kChunkGroup], cl[kChunkGroup];
@@ -296,46 +294,55 @@ __global__ void __launch_bounds__(128) attn_nodes(const AttnDev p, const float* 
       }
     }
   }
-  __syncwarp();  // qs of this warp written
 
   const float scale2 = p.sm_scale * kLog2e;
-  if (p.mask_kind == kMaskTrie) {
-    // Committed slots, in order, then the ancestors-or-self of this node in
-    // increasing index (= slot) order; every other slot is masked.
-    const int base = p.sp ? p.sp->base : p.causal_first;
-    int depth = p.depths[row];
-    if (depth < 0 || depth >= kMaxTrieDepth || depth > row) {
-      raise_device_error(0x201);
-      depth = -1;
-    }
-    if (lane == 0) {
-      int a = row;
-      for (int t = depth; t >= 0; --t) {
-        chain[warp][t] = a;
-        const int par = par_s[a];
-        if ((t > 0 && (par < 0 || par >= a)) || (t == 0 && par != -1)) {
-          raise_device_error(0x202);  // parents / depths inconsistent: fold nothing more
-          depth = -1;
-          break;
-        }
-        a = par;
-      }
-    }
-    depth = __shfl_sync(0xffffffffu, depth, 0);
-    __syncwarp();
-    const int total = base + depth + 1;
-    for (int b0 = 0; b0 < total; b0 += 32) {
+  const bool trie = p.mask_kind == kMaskTrie;
+  const int total = trie ? base + depth + 1 : p.NN;
+  for (int b0 = 0; b0 < total; b0 += 32) {
+    // 1. this batch's slots (in slot order)
+    __syncthreads();  // previous batch fully consumed
+    if (warp == 0) {
       const int i = b0 + lane;
-      const int slot = i < base ? i : (i < total ? base + chain[warp][i - base] : 0);
-      const unsigned valid = __ballot_sync(0xffffffffu, i < total);
-      fold_lanes<T>(p, kn, vn, kvh, lane, valid, slot, qs[warp], d0, scale2, m, l, acc);
+      int slot = 0;
+      bool v;
+      if (trie) {
+        v = i < total;
+        slot = i < base ? i : (v ? base + chain[i - base] : 0);
+      } else {
+        v = i < p.NN && node_allowed(p, row, i);
+        slot = i;
+      }
+      const unsigned bits = __ballot_sync(0xffffffffu, v);
+      if (v) slots[__popc(bits & ((1u << lane) - 1u))] = slot;
+      if (lane == 0) nslots = __popc(bits);
     }
-  } else {
-    // Node slots in slot order, allowed ones only (a masked slot is an exact no-op).
-    for (int j0 = 0; j0 < p.NN; j0 += 32) {
-      const int j = j0 + lane;
-      const unsigned valid = __ballot_sync(0xffffffffu, j < p.NN && node_allowed(p, row, j));
-      if (valid) fold_lanes<T>(p, kn, vn, kvh, lane, valid, j, qs[warp], d0, scale2, m, l, acc);
+    __syncthreads();
+    const int cnt = nslots;
+    if (cnt == 0) continue;
+    // 2. stage the K / V rows of the batch (16-byte pieces, all threads)
+    constexpr int kPieces = L::kRow / 16;
+    for (int t = threadIdx.x; t < cnt * kPieces; t += nthr) {
+      const int u = t / kPieces, pc = t % kPieces;
+      const int64_t sl = slots[u];
+      *reinterpret_cast<uint4*>(&ks[u][pc * 16]) =
+          *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(kn + kbase + sl * p.sknn) + pc * 16);
+      *reinterpret_cast<uint4*>(&vs[u][pc * 16]) =
+          *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(vn + vbase + sl * p.svnn) + pc * 16);
+    }
+    __syncthreads();
+    // 3. scores (lane u <- slot u), then the ordered fold
+    const float sc = lane < cnt ? dot128_smem<T>(&ks[lane][0], qs[warp]) * scale2 : 0.f;
+    for (int u = 0; u < cnt; ++u) {
+      const float su = __shfl_sync(0xffffffffu, sc, u);
+      float vv[4];
+      ld4(reinterpret_cast<const T*>(&vs[u][0]) + d0, vv);
+      const float m_new = fmaxf(m, su);
+      const float a = fast_exp2(m - m_new);
+      const float pe = fast_exp2(su - m_new);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] = fmaf(pe, vv[e], acc[e] * a);
+      l = fmaf(l, a, pe);
+      m = m_new;
     }
   }
 #pragma unroll
@@ -346,10 +353,17 @@ __global__ void __launch_bounds__(128) attn_nodes(const AttnDev p, const float* 
   }
 }
 
+template <typename T>
+static int launch_nodes(const AttnDev& p, const float* part, cudaStream_t stream, bool pdl) {
+  const int G = p.H / p.HK;
+  if (G > kMaxGroup) return RB_ERR_UNSUPPORTED;
+  return launch_k(attn_nodes<T>, dim3(p.M, p.HK), dim3(32 * G), 0, stream, pdl, p, part);
+}
+
 // ----------------------------------------------------------------- host
 size_t attn_workspace_bytes(int H, int M, int D, int NP) {
   (void)D;
-  const int nchunks = (NP + kPrefixChunk - 1) / kPrefixChunk;
+  const int nchunks = prefix_nchunks(NP, H);
   return static_cast<size_t>(nchunks > 0 ? nchunks : 1) * H * (M > 0 ? M : 1) * kPartStride * sizeof(float);
 }
 
@@ -358,6 +372,7 @@ int attn_validate(const rb_attn_args* a) {
   if (a->dtype != RB_F32 && a->dtype != RB_BF16) return RB_ERR_UNSUPPORTED;
   if (a->H <= 0 || a->HK <= 0 || a->M < 0 || a->NP < 0 || a->NN < 0) return RB_ERR_INVALID_ARG;
   if (a->H % a->HK != 0) return RB_ERR_INVALID_ARG;
+  if (a->H / a->HK > kMaxGroup) return RB_ERR_UNSUPPORTED;
   if (a->D != 128) return RB_ERR_UNSUPPORTED;
   if (a->sqd != 1 || a->sod != 1 || (a->NP > 0 && (a->skpd != 1 || a->svpd != 1)) ||
       (a->NN > 0 && (a->sknd != 1 || a->svnd != 1)))
@@ -400,7 +415,7 @@ int attn_launch(const rb_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t s
   p.out = a->out; p.soh = a->soh; p.som = a->som;
   p.sm_scale = a->sm_scale;
   float* part = static_cast<float*>(ws);
-  const int nchunks = (a->NP + kPrefixChunk - 1) / kPrefixChunk;
+  const int nchunks = prefix_nchunks(a->NP, a->H);
   if (nchunks > 0) {
     if (a->dtype == RB_F32) {  // fp32: CUDA-core FFMA (the 1e-5 parity bar rules out tf32 MMAs)
       dim3 grid(nchunks, a->H, (a->M + 15) / 16);
@@ -416,10 +431,8 @@ int attn_launch(const rb_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t s
       if (st != RB_OK) return st;
     }
   }
-  dim3 grid2((a->M + 3) / 4, a->H);
-  if (a->dtype == RB_F32) attn_nodes<float><<<grid2, 128, 0, stream>>>(p, part);
-  else attn_nodes<uint16_t><<<grid2, 128, 0, stream>>>(p, part);
-  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;
+  if (a->dtype == RB_F32) return launch_nodes<float>(p, part, stream, false);
+  return launch_nodes<uint16_t>(p, part, stream, false);
 }
 
 // Engine path: bf16, q/base/PL from device memory, trie masking from parents.
@@ -427,8 +440,7 @@ int attn_launch_engine(const AttnDev& p, float* part, int max_chunks, const CUte
                        const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t stream) {
   const int st = attn_prefix_tc_launch(tq, tk, tv, p, part, max_chunks, stream, true);
   if (st != RB_OK) return st;
-  dim3 grid2((p.M + 3) / 4, p.H);
-  return launch_k(attn_nodes<uint16_t>, grid2, dim3(128), 0, stream, true, p, static_cast<const float*>(part));
+  return launch_nodes<uint16_t>(p, part, stream, true);
 }
 
 }  // namespace rb

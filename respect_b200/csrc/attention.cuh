@@ -9,10 +9,29 @@
 
 namespace rb {
 
-// Prefix keys are reduced in chunks of this many keys at absolute positions
-// [c*kPrefixChunk, (c+1)*kPrefixChunk). A compile-time constant: results of a
-// row depend on it, so it must never vary with the call.
-constexpr int kPrefixChunk = 1024;
+// Prefix keys [0, NP) are reduced in chunks of prefix_chunk(NP, H) keys at
+// absolute positions [c*C, (c+1)*C). The chunk size depends on the prefix
+// length and the head count only (never on the number of query rows, the
+// nodes or the device), so the trie and the 1-token AR steps over the same
+// prefix split it identically. It aims at kChunkSlots / H chunks so that one
+// 128-row tile of every head fills the GPU in one wave.
+constexpr int kChunkSlots = 148;
+constexpr int kMaxChunks = 16;
+__host__ __device__ inline int prefix_chunks_target(int H) {
+  const int t = kChunkSlots / (H > 0 ? H : 1);
+  return t < 1 ? 1 : (t > kMaxChunks ? kMaxChunks : t);
+}
+__host__ __device__ inline int prefix_chunk(int NP, int H) {
+  const int t = prefix_chunks_target(H);
+  const int per = (NP + t - 1) / t;
+  const int c = ((per + 127) / 128) * 128;
+  return c < 128 ? 128 : c;
+}
+__host__ __device__ inline int prefix_nchunks(int NP, int H) {
+  if (NP <= 0) return 0;
+  const int c = prefix_chunk(NP, H);
+  return (NP + c - 1) / c;
+}
 // Per (chunk, head, row) partial: acc[128], max (log2 domain), sum, 2 pad.
 constexpr int kPartStride = 128 + 4;
 

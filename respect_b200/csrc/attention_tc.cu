@@ -1,6 +1,6 @@
 // Prefix phase of the trie attention on the 5th-generation tensor cores
 // (bf16 inputs, head_dim 128). One CTA = one query head x 128 query rows x one
-// fixed prefix chunk of kPrefixChunk keys at absolute positions; keys are
+// fixed prefix chunk of prefix_chunk(NP, H) keys at absolute positions; keys are
 // processed in tiles of 128 in ascending order (respect/kernels/attention.py:36-50):
 //
 //   S = Q K^T            tcgen05.mma, M=128 rows, N=128 keys, K=128 dims -> TMEM
@@ -56,8 +56,9 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   const int c = blockIdx.x, h = blockIdx.y, rt = blockIdx.z;
   const int NP = p.sp ? p.sp->prompt_len : p.NP;
   const int M = p.sp ? min(p.M, p.sp->q) : p.M;
-  const int k0 = c * kPrefixChunk;
-  const int k1 = min(NP, k0 + kPrefixChunk);
+  const int C = prefix_chunk(NP, p.H);
+  const int k0 = c * C;
+  const int k1 = min(NP, k0 + C);
   if (k0 >= k1 || rt * kRows >= M) return;  // uniform per CTA, before any barrier exists
   const int ntiles = (k1 - k0 + kKeys - 1) / kKeys;
   const int kvh = h / (p.H / p.HK);
@@ -173,24 +174,33 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) raw[cc][i] = 0u;
       }
-      float sv[64];
+      // Row max on the raw scores (scale2 > 0 and rounding are monotone, so
+      // max(s)*scale2 == max(s*scale2)); keys past the chunk end are masked.
       float mx = -INFINITY;
+      const bool full = nvalid >= 64;
+      if (full) {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        sv[i] = i < nvalid ? __uint_as_float(raw[i >> 4][i & 15]) * scale2 : -INFINITY;
-        mx = fmaxf(mx, sv[i]);
+        for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(raw[i >> 4][i & 15]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          if (i >= nvalid) raw[i >> 4][i & 15] = __float_as_uint(-INFINITY);
+          mx = fmaxf(mx, __uint_as_float(raw[i >> 4][i & 15]));
+        }
       }
-      red[hf * 128 + r] = mx;
+      red[hf * 128 + r] = mx * scale2;
       named_bar(1, kSoftmaxThreads);
       mx = fmaxf(red[r], red[128 + r]);
       const float m_new = fmaxf(m, mx);  // finite: every tile has a valid key in its lower half
       const float alpha = fast_exp2(m - m_new);
+      const float neg_m = -m_new;
       float rs = 0.f;
       uint32_t w[32];
 #pragma unroll
       for (int i = 0; i < 64; i += 2) {
-        const float p0 = fast_exp2(sv[i] - m_new);
-        const float p1 = fast_exp2(sv[i + 1] - m_new);
+        // p = 2^(s*scale2 - m'); a masked key (-inf) gives exactly 0
+        const float p0 = fast_exp2(fmaf(__uint_as_float(raw[i >> 4][i & 15]), scale2, neg_m));
+        const float p1 = fast_exp2(fmaf(__uint_as_float(raw[(i + 1) >> 4][(i + 1) & 15]), scale2, neg_m));
         rs += p0;
         rs += p1;
         w[i / 2] = pack_bf16x2(p0, p1);
@@ -199,7 +209,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       if (j > 0 && ok) {
         // P_{j-1} V_{j-1} must be complete before P_j overwrites P and O is rescaled.
         ok = __all_sync(0xffffffffu, mbar_wait(bar(O_FULL), (j - 1) & 1, 0x218));
-        if (ok) {
+        // alpha == 1 for every row of the warp: O * 1 == O, skip the round trip
+        if (ok && !__all_sync(0xffffffffu, alpha == 1.0f)) {
           tc_fence_after();
           const uint32_t ob = lane_base + 256 + hf * 64;
 #pragma unroll

@@ -45,9 +45,11 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
 __device__ __forceinline__ float round_bf16(float f) {
   return bf16_bits_to_f32(f32_to_bf16_bits(f));
 }
+// Two fp32 values -> bf16x2 (round to nearest even), `lo` in the low half.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  return static_cast<uint32_t>(f32_to_bf16_bits(lo)) |
-         (static_cast<uint32_t>(f32_to_bf16_bits(hi)) << 16);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 // ---------------------------------------------------------------- smem addr

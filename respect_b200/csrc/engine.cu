@@ -303,7 +303,7 @@ Layout layout_of(const rb_model_config& c) {
   if (s_lm.splits > 1) part_elems = std::max(part_elems, static_cast<size_t>(s_lm.splits) * c.vocab);
   part_elems = std::max(part_elems, static_cast<size_t>(s_o.splits) * c.hidden);
   part_elems = std::max(part_elems, static_cast<size_t>(s_d.splits) * c.hidden);
-  const int max_chunks = (c.max_slots + kPrefixChunk - 1) / kPrefixChunk;
+  const int max_chunks = prefix_chunks_target(c.n_heads);
   size_t off = 0;
   auto take = [&](size_t bytes) { const size_t o = off; off = align256(off + bytes); return o; };
   L.params = take(sizeof(StepParams));
@@ -521,7 +521,7 @@ int rb_engine_create(const rb_model_config* cfg, const rb_model_weights* w, void
   e->part = reinterpret_cast<float*>(base + L.part);
   e->apart = reinterpret_cast<float*>(base + L.apart);
   e->logits = reinterpret_cast<float*>(base + L.logits);
-  e->max_chunks = (cfg->max_slots + kPrefixChunk - 1) / kPrefixChunk;
+  e->max_chunks = prefix_chunks_target(cfg->n_heads);
 
   const rb_model_config& c = *cfg;
   const int nqkv = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
