@@ -105,6 +105,18 @@ RB_API size_t rb_linear_workspace(int M, int N, int K);
 RB_API int rb_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, void* out, int64_t ldo,
               int out_dtype, int M, int N, int K, void* workspace, size_t ws_bytes, void* stream);
 
+/* Packed weights for the weight-streaming GEMM: [ceil(N/BN)][ceil(K/64)][BN][64]
+ * bf16 (zero padded), so each pipeline stage reads one contiguous block. BN is
+ * the tile width rb_linear chooses for (N, K) (rb_linear_bn); BN <= 0 selects
+ * it. rb_linear_packed gives bitwise the same result as rb_linear on the
+ * unpacked weight (same MMA sequence per output element). No reference
+ * counterpart: a storage layout of the same linear (gemm.py:30-41). */
+RB_API int rb_linear_bn(int N, int K);
+RB_API size_t rb_linear_packed_bytes(int N, int K, int BN);
+RB_API int rb_pack_linear_weight(const void* w, int64_t ldw, int N, int K, int BN, void* out, void* stream);
+RB_API int rb_linear_packed(const void* x, int64_t ldx, const void* w_packed, void* out, int64_t ldo,
+                            int out_dtype, int M, int N, int K, void* workspace, size_t ws_bytes, void* stream);
+
 /* ------------------------------------------------------------------ rmsnorm
  * y = w * to_dtype(x * rsqrt(mean(x^2) + eps)), one row per block, fixed
  * reduction order (respect/kernels/rmsnorm.py:12-32). x, y contiguous [M, N]. */
@@ -184,19 +196,22 @@ typedef struct rb_model_config {
   int max_pos;   /* rows of the rotary tables */
 } rb_model_config;
 
-/* Per layer, bf16 device pointers:
+/* Per layer, bf16 device pointers. The four projection matrices are given in
+ * the packed layout of rb_pack_linear_weight (BN = rb_linear_bn(N, K), except
+ * wgu: BN = 256) of these logical [N, K] matrices:
  *   wqkv [(n_heads + 2 n_kv_heads) * 128, hidden]   q_proj | k_proj | v_proj rows
  *   wo   [hidden, n_heads * 128]
- *   wgu  [2 ffn, hidden]  gate_proj and up_proj packed in 128-row blocks:
+ *   wgu  [2 ffn, hidden]  gate_proj and up_proj interleaved in 128-row blocks:
  *        rows [256 b, 256 b + 128) = gate rows [128 b, 128 b + 128),
  *        rows [256 b + 128, 256 b + 256) = up rows [128 b, 128 b + 128)
  *   wd   [hidden, ffn]
- *   in_norm, post_norm [hidden]; q_norm, k_norm [128] */
+ *   in_norm, post_norm [hidden]; q_norm, k_norm [128] (plain vectors) */
 typedef struct rb_layer_weights {
   const void *wqkv, *wo, *wgu, *wd, *in_norm, *post_norm, *q_norm, *k_norm;
 } rb_layer_weights;
 
-/* embed, lm_head [vocab, hidden] bf16; final_norm [hidden] bf16; rope_cos /
+/* embed [vocab, hidden] bf16 (row-major), lm_head [vocab, hidden] bf16 packed
+ * (rb_pack_linear_weight, BN = rb_linear_bn(vocab, hidden)); final_norm [hidden] bf16; rope_cos /
  * rope_sin [max_pos, 128] bf16 (the model's rotary table cast to bf16);
  * layers: host array of n_layers; k_cache / v_cache: host arrays of n_layers
  * device buffers, each [n_kv_heads, max_slots, 128] bf16 contiguous. */

@@ -60,6 +60,11 @@ SIGNATURES = {
     "rb_linear_workspace": (c_size_t, [c_int, c_int, c_int]),
     "rb_linear": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_int,
                           c_int, c_void_p, c_size_t, c_void_p]),
+    "rb_linear_bn": (c_int, [c_int, c_int]),
+    "rb_linear_packed_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "rb_pack_linear_weight": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "rb_linear_packed": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_int,
+                                 c_void_p, c_size_t, c_void_p]),
     "rb_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_int, c_int, c_void_p]),
     "rb_rope": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                         c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),

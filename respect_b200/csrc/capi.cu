@@ -83,6 +83,51 @@ int rb_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, void* out,
   return splitk_reduce(a.partial, s.splits, M, N, out, ldo, out_dtype == RB_F32, st);
 }
 
+int rb_linear_bn(int N, int K) {
+  if (N <= 0 || K <= 0) return 0;
+  return gemm_plan(1, N, K, device_sm_count()).BN;
+}
+
+size_t rb_linear_packed_bytes(int N, int K, int BN) {
+  if (N <= 0 || K <= 0) return 0;
+  if (BN <= 0) BN = rb_linear_bn(N, K);
+  return gemm_packed_elems(N, K, BN) * 2;
+}
+
+int rb_pack_linear_weight(const void* w, int64_t ldw, int N, int K, int BN, void* out, void* stream) {
+  if (BN <= 0) BN = rb_linear_bn(N, K);
+  return gemm_pack_weight(w, ldw, N, K, BN, out, as_stream(stream));
+}
+
+int rb_linear_packed(const void* x, int64_t ldx, const void* wp, void* out, int64_t ldo, int out_dtype, int M, int N,
+                     int K, void* workspace, size_t ws_bytes, void* stream) {
+  if (M < 0 || N <= 0 || K <= 0 || !x || !wp || !out) return RB_ERR_INVALID_ARG;
+  if (out_dtype != RB_BF16 && out_dtype != RB_F32) return RB_ERR_UNSUPPORTED;
+  if (M == 0) return RB_OK;
+  if (K % 8 != 0 || ldx % 8 != 0 || ldx < K || ldo < N) return RB_ERR_UNSUPPORTED;
+  if (!aligned16(x) || !aligned16(wp) || !aligned16(out)) return RB_ERR_UNSUPPORTED;
+  const GemmShape s = gemm_plan(M, N, K, device_sm_count());
+  CUtensorMap mx, mw;
+  int r = gemm_encode_x(&mx, x, M, K, ldx);
+  if (r != RB_OK) return r;
+  r = gemm_encode_w_packed(&mw, wp, N, K, s.BN);
+  if (r != RB_OK) return r;
+  GemmLaunch a{};
+  a.x = x; a.ldx = ldx; a.w = wp; a.out = out; a.ldo = ldo; a.w_tiled = 1;
+  cudaStream_t st = as_stream(stream);
+  if (s.splits == 1) {
+    a.epi = out_dtype == RB_F32 ? kEpiStoreF32 : kEpiStoreBF16;
+    return gemm_launch_maps(s, mx, mw, a, st);
+  }
+  const size_t need = static_cast<size_t>(s.splits) * M * N * sizeof(float);
+  if (!workspace || ws_bytes < need || !aligned16(workspace)) return RB_ERR_WORKSPACE;
+  a.epi = kEpiPartial;
+  a.partial = static_cast<float*>(workspace);
+  r = gemm_launch_maps(s, mx, mw, a, st);
+  if (r != RB_OK) return r;
+  return splitk_reduce(a.partial, s.splits, M, N, out, ldo, out_dtype == RB_F32, st);
+}
+
 // ------------------------------------------------------------------ rmsnorm / rope / silu
 int rb_rmsnorm(const void* x, const void* w, void* y, int M, int N, float eps, int x_dtype, int w_dtype,
                void* stream) {

@@ -404,6 +404,7 @@ int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
   for (int l = 0; l < c.n_layers; ++l) {
     const rb_layer_weights& lw = e->layers[l];
     GemmLaunch g{};
+    g.w_tiled = 1;
     // q|k|v projection
     g.epi = kEpiPartial;
     g.partial = e->part;
@@ -440,6 +441,7 @@ int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
     RB_TRY(launch_resid_norm(e, s_o.splits, rows, lw.post_norm, st));
     // gate|up with the SiLU*mul epilogue
     GemmLaunch gu{};
+    gu.w_tiled = 1;
     gu.epi = kEpiSiluMul;
     gu.out = e->act;
     gu.ldo = c.ffn;
@@ -453,6 +455,7 @@ int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
   // lm_head (fp32 scores) with the greedy choice (acceptance.py:11-23) folded in;
   // the keys are zero on entry (zeroed at set-up, reset by the finalize kernel).
   GemmLaunch gl{};
+  gl.w_tiled = 1;
   if (s_lm.splits == 1) {
     gl.epi = kEpiF32Argmax;
     gl.out = e->logits;
@@ -547,15 +550,15 @@ int rb_engine_create(const rb_model_config* cfg, const rb_model_weights* w, void
       st = RB_ERR_INVALID_ARG;
       break;
     }
-    st |= gemm_encode_w(&e->m_qkv[l], lw.wqkv, nqkv, c.hidden, c.hidden, s_qkv.BN);
-    st |= gemm_encode_w(&e->m_o[l], lw.wo, c.hidden, c.n_heads * c.head_dim, c.n_heads * c.head_dim, s_o.BN);
-    st |= gemm_encode_w(&e->m_gu[l], lw.wgu, 2 * c.ffn, c.hidden, c.hidden, 256);
-    st |= gemm_encode_w(&e->m_d[l], lw.wd, c.hidden, c.ffn, c.ffn, s_d.BN);
+    st |= gemm_encode_w_packed(&e->m_qkv[l], lw.wqkv, nqkv, c.hidden, s_qkv.BN);
+    st |= gemm_encode_w_packed(&e->m_o[l], lw.wo, c.hidden, c.n_heads * c.head_dim, s_o.BN);
+    st |= gemm_encode_w_packed(&e->m_gu[l], lw.wgu, 2 * c.ffn, c.hidden, 256);
+    st |= gemm_encode_w_packed(&e->m_d[l], lw.wd, c.hidden, c.ffn, s_d.BN);
     const int64_t sh = static_cast<int64_t>(c.max_slots) * c.head_dim;
     st |= encode_heads_3d(&e->m_kc[l], e->kc[l], c.max_slots, c.n_kv_heads, c.head_dim, sh);
     st |= encode_heads_3d(&e->m_vc[l], e->vc[l], c.max_slots, c.n_kv_heads, c.head_dim, sh);
   }
-  if (st == RB_OK) st = gemm_encode_w(&e->m_lm, w->lm_head, c.vocab, c.hidden, c.hidden, s_lm.BN);
+  if (st == RB_OK) st = gemm_encode_w_packed(&e->m_lm, w->lm_head, c.vocab, c.hidden, s_lm.BN);
   if (st != RB_OK) {
     delete e;
     return st != RB_ERR_INVALID_ARG ? RB_ERR_UNSUPPORTED : st;

@@ -36,6 +36,7 @@ struct GemmCfg {
 struct GemmKernelArgs {
   int M, N, K;
   int k_chunks, splits;
+  int w_tiled;  // weights packed as [n_tile][k_chunk][BN][64] (gemm_pack_weight)
   void* out;
   int64_t ldo;
   float* partial;
@@ -146,10 +147,13 @@ __global__ void __launch_bounds__(128, 1)
     const uint64_t pol_w = policy_evict_first();
     const uint64_t pol_x = policy_evict_last();
     const int npre = nk < C::kStages ? nk : C::kStages;
+    // weight tile coordinates: row-major [N, K] or packed tiles (contiguous 32 KB blocks)
+    auto wx = [&](int kc) { return a.w_tiled ? 0 : kc * kBK; };
+    auto wy = [&](int kc) { return a.w_tiled ? (n_tile * a.k_chunks + kc) * BN : n_tile * BN; };
     for (int i = 0; i < npre; ++i) {
       mbar_arrive_expect_tx(full0 + 8 * i, C::kStageBytes);
-      tma_load_2d(smem_u32(smem + i * C::kStageBytes) + MT * kXTileBytes, &tmw, full0 + 8 * i, (kc0 + i) * kBK,
-                  n_tile * BN, pol_w);
+      tma_load_2d(smem_u32(smem + i * C::kStageBytes) + MT * kXTileBytes, &tmw, full0 + 8 * i, wx(kc0 + i),
+                  wy(kc0 + i), pol_w);
     }
     pdl_wait();
     for (int i = 0; i < npre; ++i) {
@@ -168,7 +172,7 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
         tma_load_2d(st + mt * kXTileBytes, &tmx, full0 + 8 * s, kx, (m_group * MT + mt) * kTileM, pol_x);
-      tma_load_2d(st + MT * kXTileBytes, &tmw, full0 + 8 * s, kx, n_tile * BN, pol_w);
+      tma_load_2d(st + MT * kXTileBytes, &tmw, full0 + 8 * s, wx(kc0 + i), wy(kc0 + i), pol_w);
     }
   } else if (warp == 1 && lane == 0) {
     // MMA issuer: 4 K-steps of 16 per stage, one MMA per token tile per step.
@@ -298,6 +302,44 @@ int gemm_encode_w(CUtensorMap* m, const void* w, int N, int K, int64_t ldw, int 
   return encode_2d_bf16(m, w, K, N, ldw, kBK, BN);
 }
 
+size_t gemm_packed_elems(int N, int K, int BN) {
+  const size_t nt = (N + BN - 1) / BN, kc = (K + kBK - 1) / kBK;
+  return nt * kc * BN * kBK;
+}
+
+int gemm_encode_w_packed(CUtensorMap* m, const void* wp, int N, int K, int BN) {
+  const uint64_t rows = gemm_packed_elems(N, K, BN) / kBK;
+  return encode_2d_bf16(m, wp, kBK, rows, kBK, kBK, BN);
+}
+
+// out[((nt*KC + kc)*BN + r)*64 + c] = w[nt*BN + r][kc*64 + c] (zero outside [N, K]).
+__global__ void pack_weight_kernel(const uint16_t* __restrict__ w, int64_t ldw, int N, int K, int BN, int KC,
+                                   uint16_t* __restrict__ out, int64_t pieces) {
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= pieces) return;
+  const int c8 = static_cast<int>(t % (kBK / 8));
+  const int64_t row = t / (kBK / 8);  // packed row = (nt*KC + kc)*BN + r
+  const int r = static_cast<int>(row % BN);
+  const int64_t tk = row / BN;
+  const int kc = static_cast<int>(tk % KC);
+  const int nt = static_cast<int>(tk / KC);
+  const int n = nt * BN + r, k = kc * kBK + c8 * 8;
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  if (n < N && k < K) v = *reinterpret_cast<const uint4*>(w + static_cast<int64_t>(n) * ldw + k);  // K % 8 == 0
+  *reinterpret_cast<uint4*>(out + row * kBK + c8 * 8) = v;
+}
+
+int gemm_pack_weight(const void* w, int64_t ldw, int N, int K, int BN, void* out, cudaStream_t st) {
+  if (!w || !out || N <= 0 || K <= 0 || K % 8 || ldw % 8 || ldw < K || BN % 16 || BN < 16 || BN > 256)
+    return RB_ERR_INVALID_ARG;
+  if (!aligned16(w) || !aligned16(out)) return RB_ERR_UNSUPPORTED;
+  const int KC = (K + kBK - 1) / kBK;
+  const int64_t pieces = static_cast<int64_t>(gemm_packed_elems(N, K, BN) / 8);
+  pack_weight_kernel<<<static_cast<unsigned>((pieces + 255) / 256), 256, 0, st>>>(
+      static_cast<const uint16_t*>(w), ldw, N, K, BN, KC, static_cast<uint16_t*>(out), pieces);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;
+}
+
 template <int BN, int MT, int EPI>
 static int launch_t(const GemmShape& s, const CUtensorMap& mx, const CUtensorMap& mw,
                     const GemmKernelArgs& ka, cudaStream_t stream, bool pdl) {
@@ -328,6 +370,7 @@ int gemm_launch_maps(const GemmShape& s, const CUtensorMap& mx, const CUtensorMa
   ka.M = s.M; ka.N = s.N; ka.K = s.K;
   ka.k_chunks = s.k_chunks;
   ka.splits = s.splits;
+  ka.w_tiled = a.w_tiled;
   ka.out = a.out;
   ka.ldo = a.ldo;
   ka.partial = a.partial;

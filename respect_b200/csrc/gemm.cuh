@@ -65,6 +65,7 @@ struct GemmLaunch {
   int epi;
   unsigned long long* keys;     // kEpiF32Argmax: [M] per-row keys (caller zeroes them)
   const int* excl;              // kEpiF32Argmax: {offset, size} of the excluded column range (device)
+  int w_tiled;                  // w is packed (gemm_pack_weight) and its map from gemm_encode_w_packed
 };
 
 // Encodes the tensor maps and launches. Returns an rb_status code.
@@ -77,6 +78,13 @@ int gemm_launch_maps(const GemmShape& s, const CUtensorMap& mx, const CUtensorMa
                      const GemmLaunch& a, cudaStream_t stream, bool pdl = false);
 int gemm_encode_x(CUtensorMap* m, const void* x, int M, int K, int64_t ldx);
 int gemm_encode_w(CUtensorMap* m, const void* w, int N, int K, int64_t ldw, int BN);
+
+// Packed weights: [ceil(N/BN)][ceil(K/64)][BN][64] bf16, zero padded, so each
+// pipeline stage streams one contiguous BN x 128-byte block. The MMA sequence
+// per output element is the same as with the row-major layout.
+size_t gemm_packed_elems(int N, int K, int BN);
+int gemm_encode_w_packed(CUtensorMap* m, const void* wp, int N, int K, int BN);
+int gemm_pack_weight(const void* w, int64_t ldw, int N, int K, int BN, void* out, cudaStream_t st);
 
 // Sum split partials in ascending split order and store (bf16 or fp32).
 int splitk_reduce(const float* partial, int splits, int M, int N, void* out, int64_t ldo,

@@ -178,12 +178,18 @@ class VerifyEngine:
         if nbytes == 0:
             raise ValueError(f"respect_b200 engine does not support {c}")
         self.ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        # projection weights in the packed tile layout (gate|up with 256-row tiles)
+        from respect_b200.kernels.gemm import pack_weight
+        self.packed = [dict(wqkv=pack_weight(lw["wqkv"]), wo=pack_weight(lw["wo"]), wgu=pack_weight(lw["wgu"], 256),
+                            wd=pack_weight(lw["wd"])) for lw in weights.layers]
+        self.lm_packed = pack_weight(weights.lm_head)
         self._layers = (_LayerW * c.n_layers)(*[
-            _LayerW(*(lw[k].data_ptr() for k in ("wqkv", "wo", "wgu", "wd", "in_norm", "post_norm",
-                                                 "q_norm", "k_norm"))) for lw in weights.layers])
+            _LayerW(pk["wqkv"].data_ptr(), pk["wo"].data_ptr(), pk["wgu"].data_ptr(), pk["wd"].data_ptr(),
+                    *(lw[k].data_ptr() for k in ("in_norm", "post_norm", "q_norm", "k_norm")))
+            for pk, lw in zip(self.packed, weights.layers)])
         self._kp = (ctypes.c_void_p * c.n_layers)(*[t.data_ptr() for t in self.kc])
         self._vp = (ctypes.c_void_p * c.n_layers)(*[t.data_ptr() for t in self.vc])
-        mw = _ModelW(weights.embed.data_ptr(), weights.final_norm.data_ptr(), weights.lm_head.data_ptr(),
+        mw = _ModelW(weights.embed.data_ptr(), weights.final_norm.data_ptr(), self.lm_packed.data_ptr(),
                      self.cos.data_ptr(), self.sin.data_ptr(), self._layers, self._kp, self._vp)
         h = ctypes.c_void_p()
         with torch.cuda.device(self.device):

@@ -30,3 +30,30 @@ def linear(x, w, BM=32, BN=128, BK=64, num_warps=4, num_stages=2, out_dtype=None
               out.stride(0), _lib.dtype_code(od), M, N, K,
               ws.data_ptr() if ws is not None else None, nbytes, _lib.stream_of(xs))
     return out.reshape(*x.shape[:-1], N)
+
+
+def pack_weight(w: torch.Tensor, bn: int = 0) -> torch.Tensor:
+    """Copy of w [N, K] (bf16) in the packed tile layout the weight-streaming
+    kernel reads contiguously: [ceil(N/BN)][ceil(K/64)][BN][64], zero padded.
+    bn=0 uses the tile width linear() picks for (N, K)."""
+    N, K = w.shape
+    if w.stride(-1) != 1:
+        w = w.contiguous()
+    nbytes = _lib.lib().rb_linear_packed_bytes(N, K, bn)
+    out = torch.empty(nbytes // 2, dtype=torch.bfloat16, device=w.device)
+    _lib.call("rb_pack_linear_weight", w.data_ptr(), w.stride(0), N, K, bn, out.data_ptr(), _lib.stream_of(w))
+    return out
+
+
+def linear_packed(x, w_packed, N, out_dtype=None):
+    """linear(x, w) for a weight packed by pack_weight(w) (bn=0): bitwise equal results."""
+    K = x.shape[-1]
+    xs = x.reshape(-1, K).contiguous()
+    M = xs.shape[0]
+    od = out_dtype or x.dtype
+    out = torch.empty((M, N), device=x.device, dtype=od)
+    nbytes = _lib.lib().rb_linear_workspace(M, N, K)
+    ws = _lib.workspace(xs, nbytes)
+    _lib.call("rb_linear_packed", xs.data_ptr(), xs.stride(0), w_packed.data_ptr(), out.data_ptr(), out.stride(0),
+              _lib.dtype_code(od), M, N, K, ws.data_ptr() if ws is not None else None, nbytes, _lib.stream_of(xs))
+    return out.reshape(*x.shape[:-1], N)

@@ -168,6 +168,18 @@ def test_linear_row_count_invariance():
             assert torch.equal(linear(x[:m], w), full[:m])
 
 
+@pytest.mark.parametrize("M,N,K", [(128, 4608, 3584), (1, 3584, 18944), (200, 37888, 512), (33, 152064, 256),
+                                   (5, 1000, 200)])
+def test_linear_packed_is_bitwise_linear(M, N, K):
+    from respect_b200.kernels.gemm import linear, linear_packed, pack_weight
+    g = torch.Generator(device=DEV).manual_seed(N + K)
+    x = torch.randn(M, K, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=DEV, generator=g) * 0.05).to(torch.bfloat16)
+    wp = pack_weight(w)
+    for od in (None, torch.float32):
+        assert torch.equal(linear_packed(x, wp, N, out_dtype=od), linear(x, w, out_dtype=od))
+
+
 # ---------------------------------------------------------------- rmsnorm / rope / silu
 @pytest.mark.parametrize("N", [128, 384, 3584, 4096])
 def test_rmsnorm_vs_oracle_and_row_invariance(N):
