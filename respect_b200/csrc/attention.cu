@@ -204,11 +204,14 @@ __global__ void __launch_bounds__(32 * kMaxGroup) attn_nodes(const AttnDev p, co
   constexpr int D = 128;
   using L = NodeSmem<T>;
   __shared__ int chain[kMaxTrieDepth];
+  __shared__ int par_s[kMaxTrieDepth];
   __shared__ int slots[32];
   __shared__ int nslots;
   __shared__ __align__(16) float qs[kMaxGroup][D];
-  __shared__ __align__(16) uint8_t ks[32][L::kKPitch];
-  __shared__ __align__(16) uint8_t vs[32][L::kRow];
+  // node K / V rows of the current batch (dynamic shared memory: 32 x (kKPitch + kRow) bytes)
+  extern __shared__ __align__(16) uint8_t node_smem[];
+  auto ks = reinterpret_cast<uint8_t(*)[L::kKPitch]>(node_smem);
+  auto vs = reinterpret_cast<uint8_t(*)[L::kRow]>(node_smem + 32 * L::kKPitch);
   const int G = p.H / p.HK;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x, kvh = blockIdx.y;
@@ -239,6 +242,9 @@ __global__ void __launch_bounds__(32 * kMaxGroup) attn_nodes(const AttnDev p, co
   int base = 0, depth = -1;
   if (p.mask_kind == kMaskTrie) {
     base = p.sp ? p.sp->base : p.causal_first;
+    // parents of nodes 0..row, then the pointer chase runs in shared memory
+    for (int i = threadIdx.x; i <= row && i < kMaxTrieDepth; i += nthr) par_s[i] = p.parents[i];
+    __syncthreads();
     if (threadIdx.x == 0) {
       int dd = p.depths[row];
       if (dd < 0 || dd >= kMaxTrieDepth || dd > row) {
@@ -248,7 +254,7 @@ __global__ void __launch_bounds__(32 * kMaxGroup) attn_nodes(const AttnDev p, co
       int a = row;
       for (int t = dd; t >= 0; --t) {
         chain[t] = a;
-        const int par = p.parents[a];
+        const int par = par_s[a];
         if ((t > 0 && (par < 0 || par >= a)) || (t == 0 && par != -1)) {
           raise_device_error(0x202);  // parents / depths inconsistent: fold nothing more
           dd = -1;
@@ -357,7 +363,11 @@ template <typename T>
 static int launch_nodes(const AttnDev& p, const float* part, cudaStream_t stream, bool pdl) {
   const int G = p.H / p.HK;
   if (G > kMaxGroup) return RB_ERR_UNSUPPORTED;
-  return launch_k(attn_nodes<T>, dim3(p.M, p.HK), dim3(32 * G), 0, stream, pdl, p, part);
+  using L = NodeSmem<T>;
+  constexpr int dyn = 32 * (L::kKPitch + L::kRow);
+  if (cudaFuncSetAttribute(attn_nodes<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) != cudaSuccess)
+    return RB_ERR_CUDA;
+  return launch_k(attn_nodes<T>, dim3(p.M, p.HK), dim3(32 * G), dyn, stream, pdl, p, part);
 }
 
 // ----------------------------------------------------------------- host

@@ -22,9 +22,10 @@ template <> struct IsBF16<uint16_t> { static constexpr bool value = true; };
 // Rounding points follow PyTorch: upcast, mean of squares, rsqrt, downcast to
 // the input dtype, multiply by the weight, downcast.
 template <typename TX, typename TW, int NT>
-__global__ void rmsnorm_kernel(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restrict__ y,
-                               int M, int N, float eps) {
-  constexpr int kRowsPerBlock = 256 / NT;  // blocks are always 256 threads
+__global__ void __launch_bounds__(NT >= 256 ? NT : 256) rmsnorm_kernel(const TX* __restrict__ x,
+                                                                      const TW* __restrict__ w,
+                                                                      TX* __restrict__ y, int M, int N, float eps) {
+  constexpr int kRowsPerBlock = NT >= 256 ? 1 : 256 / NT;  // blocks of max(NT, 256) threads
   constexpr int kWarps = NT / 32;
   __shared__ float red[kRowsPerBlock][kWarps];
   const int sub = threadIdx.x / NT, t = threadIdx.x % NT;
@@ -62,7 +63,7 @@ static int rmsnorm_t(const void* x, const void* w, void* y, int M, int N, float 
   if (M <= 0) return RB_OK;
   // Threads per row depend on N only.
   if (N >= 2048) {
-    rmsnorm_kernel<TX, TW, 256><<<M, 256, 0, s>>>(xp, wp, yp, M, N, eps);
+    rmsnorm_kernel<TX, TW, 1024><<<M, 1024, 0, s>>>(xp, wp, yp, M, N, eps);
   } else if (N >= 512) {
     rmsnorm_kernel<TX, TW, 128><<<(M + 1) / 2, 256, 0, s>>>(xp, wp, yp, M, N, eps);
   } else {

@@ -48,7 +48,7 @@ __device__ __forceinline__ float row_inv_rms(const float* v, int cnt, int N, flo
   return rsqrtf(tot / static_cast<float>(N) + eps);
 }
 
-constexpr int kMaxPerThread = 32;  // hidden <= 32 * NT
+constexpr int kMaxPerThread = 32;  // hidden <= 32 * NT (NT = 1024 for hidden >= 2048)
 
 // h[row] = embed[ids[row]];  xn[row] = rmsnorm(h[row], w). EPT: elements per thread.
 template <int NT, int EPT>
@@ -331,7 +331,7 @@ int validate_cfg(const rb_model_config* c) {
     return RB_ERR_INVALID_ARG;
   if (c->head_dim != 128 || c->n_heads % c->n_kv_heads != 0) return RB_ERR_UNSUPPORTED;
   if (c->hidden % 64 != 0 || c->ffn % 128 != 0 || c->vocab % 8 != 0) return RB_ERR_UNSUPPORTED;
-  if (c->hidden > kMaxPerThread * 256) return RB_ERR_UNSUPPORTED;
+  if (c->hidden > kMaxPerThread * 1024) return RB_ERR_UNSUPPORTED;
   if (c->max_rows > 1024 || c->n_layers > RB_COMPACT_MAX_LAYERS) return RB_ERR_CAPACITY;
   return RB_OK;
 }
@@ -351,7 +351,7 @@ int launch_norm_ept(int N, F&& f) {
 }
 template <typename F>
 int launch_norm_nt(int N, F&& f) {
-  if (N >= 2048) return launch_norm_ept<256>(N, f);
+  if (N >= 2048) return launch_norm_ept<1024>(N, f);
   if (N >= 512) return launch_norm_ept<128>(N, f);
   return launch_norm_ept<32>(N, f);
 }

@@ -37,6 +37,7 @@ struct GemmKernelArgs {
   int M, N, K;
   int k_chunks, splits;
   int w_tiled;  // weights packed as [n_tile][k_chunk][BN][64] (gemm_pack_weight)
+
   void* out;
   int64_t ldo;
   float* partial;
@@ -371,6 +372,7 @@ int gemm_launch_maps(const GemmShape& s, const CUtensorMap& mx, const CUtensorMa
   ka.k_chunks = s.k_chunks;
   ka.splits = s.splits;
   ka.w_tiled = a.w_tiled;
+
   ka.out = a.out;
   ka.ldo = a.ldo;
   ka.partial = a.partial;
