@@ -19,18 +19,26 @@ __host__ __device__ constexpr int pow2_cols(int c) {
   return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512;
 }
 
+// Shared memory: a ring of weight tiles (BN x 64, the DRAM stream, as deep as
+// fits) and a short ring of token tiles (MT x 128 x 64, L2-resident).
 template <int BN, int MT>
 struct GemmCfg {
   static constexpr int kWTileBytes = BN * kBK * 2;
-  static constexpr int kStageBytes = MT * kXTileBytes + kWTileBytes;
-  static constexpr int kStagesRaw = (kSmemLimit - 1024 - 256) / kStageBytes;
-  static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
+  static constexpr int kXStageBytes = MT * kXTileBytes;
+  static constexpr int kXStages = 2;
+  static constexpr int kWStagesRaw = (kSmemLimit - 1024 - 256 - kXStages * kXStageBytes) / kWTileBytes;
+  static constexpr int kWStages = kWStagesRaw > 8 ? 8 : kWStagesRaw;
+  static constexpr int kWOff = 0;
+  static constexpr int kXOff = kWStages * kWTileBytes;
+  static constexpr int kBarOff = kXOff + kXStages * kXStageBytes;
   static constexpr int kAccStride = pow2_cols(BN);  // TMEM columns between token-tile accumulators
   static constexpr int kTmemCols = MT * kAccStride;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;
+  static constexpr int kSmemBytes = 1024 + kBarOff + 256;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 is 16..256 step 16");
   static_assert(MT * pow2_cols(BN) <= 512, "TMEM holds 512 fp32 columns");
-  static_assert(kStages >= 2, "pipeline needs two stages");
+  static_assert(kWStages >= 3, "weight ring needs three stages");
+  static_assert(kWTileBytes % 1024 == 0 && kXTileBytes % 1024 == 0, "swizzle atoms are 1024-byte aligned");
+  static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
 };
 
 struct GemmKernelArgs {
@@ -108,11 +116,15 @@ __global__ void __launch_bounds__(128, 1)
   using C = GemmCfg<BN, MT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::kStages + 1);
-  const uint32_t full0 = smem_u32(bars);
-  const uint32_t empty0 = smem_u32(bars + C::kStages);
-  const uint32_t accum = smem_u32(bars + 2 * C::kStages);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  // barriers: wfull[kWStages], wempty[kWStages], xfull[2], xempty[2], accum
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::kWStages + 2 * C::kXStages + 1);
+  const uint32_t wfull0 = smem_u32(bars);
+  const uint32_t wempty0 = smem_u32(bars + C::kWStages);
+  const uint32_t xfull0 = smem_u32(bars + 2 * C::kWStages);
+  const uint32_t xempty0 = smem_u32(bars + 2 * C::kWStages + C::kXStages);
+  const uint32_t accum = smem_u32(bars + 2 * C::kWStages + 2 * C::kXStages);
+  const uint32_t sW = smem_u32(smem + C::kWOff), sX = smem_u32(smem + C::kXOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tile = blockIdx.x, split = blockIdx.y, m_group = blockIdx.z;
@@ -124,9 +136,13 @@ __global__ void __launch_bounds__(128, 1)
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmx);
     tma_prefetch_desc(&tmw);
-    for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(full0 + 8 * s, 1);
-      mbar_init(empty0 + 8 * s, 1);
+    for (int s = 0; s < C::kWStages; ++s) {
+      mbar_init(wfull0 + 8 * s, 1);
+      mbar_init(wempty0 + 8 * s, 1);
+    }
+    for (int s = 0; s < C::kXStages; ++s) {
+      mbar_init(xfull0 + 8 * s, 1);
+      mbar_init(xempty0 + 8 * s, 1);
     }
     mbar_init(accum, 1);
     fence_mbar_init();
@@ -141,60 +157,54 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0 && lane == 0) {
-    // TMA producer: one stage = MT token tiles + one weight tile, 64 K-elements.
-    // The weight tiles of the first stages do not depend on the previous
-    // kernel: they are requested before waiting for it (PDL), the token tiles
-    // after.
+    // Weight producer: contiguous BN x 64 tiles, kWStages deep. Weights never
+    // depend on the previous kernel, so this thread does not wait for it (PDL).
     const uint64_t pol_w = policy_evict_first();
-    const uint64_t pol_x = policy_evict_last();
-    const int npre = nk < C::kStages ? nk : C::kStages;
-    // weight tile coordinates: row-major [N, K] or packed tiles (contiguous 32 KB blocks)
-    auto wx = [&](int kc) { return a.w_tiled ? 0 : kc * kBK; };
-    auto wy = [&](int kc) { return a.w_tiled ? (n_tile * a.k_chunks + kc) * BN : n_tile * BN; };
-    for (int i = 0; i < npre; ++i) {
-      mbar_arrive_expect_tx(full0 + 8 * i, C::kStageBytes);
-      tma_load_2d(smem_u32(smem + i * C::kStageBytes) + MT * kXTileBytes, &tmw, full0 + 8 * i, wx(kc0 + i),
-                  wy(kc0 + i), pol_w);
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % C::kWStages;
+      if (i >= C::kWStages && !mbar_wait(wempty0 + 8 * s, ((i / C::kWStages) & 1) ^ 1, 0x101)) break;
+      const int kc = kc0 + i;
+      mbar_arrive_expect_tx(wfull0 + 8 * s, C::kWTileBytes);
+      tma_load_2d(sW + s * C::kWTileBytes, &tmw, wfull0 + 8 * s, a.w_tiled ? 0 : kc * kBK,
+                  a.w_tiled ? (n_tile * a.k_chunks + kc) * BN : n_tile * BN, pol_w);
     }
+  } else if (warp == 3 && lane == 0) {
+    // Token producer: the activations come from the previous kernel.
     pdl_wait();
-    for (int i = 0; i < npre; ++i) {
+    const uint64_t pol_x = policy_evict_last();
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % C::kXStages;
+      if (i >= C::kXStages && !mbar_wait(xempty0 + 8 * s, ((i / C::kXStages) & 1) ^ 1, 0x104)) break;
+      mbar_arrive_expect_tx(xfull0 + 8 * s, C::kXStageBytes);
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
-        tma_load_2d(smem_u32(smem + i * C::kStageBytes) + mt * kXTileBytes, &tmx, full0 + 8 * i, (kc0 + i) * kBK,
+        tma_load_2d(sX + s * C::kXStageBytes + mt * kXTileBytes, &tmx, xfull0 + 8 * s, (kc0 + i) * kBK,
                     (m_group * MT + mt) * kTileM, pol_x);
-    }
-    for (int i = npre; i < nk; ++i) {
-      const int s = i % C::kStages;
-      const uint32_t ph = (i / C::kStages) & 1;
-      if (!mbar_wait(empty0 + 8 * s, ph ^ 1, 0x101)) break;
-      const uint32_t st = smem_u32(smem + s * C::kStageBytes);
-      mbar_arrive_expect_tx(full0 + 8 * s, C::kStageBytes);
-      const int kx = (kc0 + i) * kBK;
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
-        tma_load_2d(st + mt * kXTileBytes, &tmx, full0 + 8 * s, kx, (m_group * MT + mt) * kTileM, pol_x);
-      tma_load_2d(st + MT * kXTileBytes, &tmw, full0 + 8 * s, wx(kc0 + i), wy(kc0 + i), pol_w);
     }
   } else if (warp == 1 && lane == 0) {
     // MMA issuer: 4 K-steps of 16 per stage, one MMA per token tile per step.
     constexpr uint32_t idesc = idesc_bf16_f32(kTileM, BN);
     bool ok = true;
     for (int i = 0; i < nk; ++i) {
-      const int s = i % C::kStages;
-      const uint32_t ph = (i / C::kStages) & 1;
-      if (!mbar_wait(full0 + 8 * s, ph, 0x102)) { ok = false; break; }
+      const int sw = i % C::kWStages, sx = i % C::kXStages;
+      if (!mbar_wait(wfull0 + 8 * sw, (i / C::kWStages) & 1, 0x102) ||
+          !mbar_wait(xfull0 + 8 * sx, (i / C::kXStages) & 1, 0x105)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      const uint32_t st = smem_u32(smem + s * C::kStageBytes);
 #pragma unroll
       for (int kk = 0; kk < kBK / 16; ++kk) {
-        const uint64_t bdesc = sdesc_kmajor_sw128(st + MT * kXTileBytes + kk * 32);
+        const uint64_t bdesc = sdesc_kmajor_sw128(sW + sw * C::kWTileBytes + kk * 32);
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
-          const uint64_t adesc = sdesc_kmajor_sw128(st + mt * kXTileBytes + kk * 32);
+          const uint64_t adesc = sdesc_kmajor_sw128(sX + sx * C::kXStageBytes + mt * kXTileBytes + kk * 32);
           umma_bf16(tmem + mt * C::kAccStride, adesc, bdesc, idesc, (i | kk) != 0 ? 1u : 0u);
         }
       }
-      umma_commit(empty0 + 8 * s);
+      // free the stages for the producers (only stages that will be refilled)
+      if (i + C::kWStages < nk) umma_commit(wempty0 + 8 * sw);
+      if (i + C::kXStages < nk) umma_commit(xempty0 + 8 * sx);
     }
     if (ok) umma_commit(accum);
   }
