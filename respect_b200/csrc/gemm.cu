@@ -109,8 +109,13 @@ __device__ __forceinline__ float silu_mul_bf16(float g_acc, float u_acc) {
   return __fmul_rn(s, u);
 }
 
+// 256 threads: warps 0-3 run the pipeline (weight producer, MMA, TMEM owner,
+// token producer); in the epilogue all 8 warps drain TMEM, warp w serving
+// lanes 32*(w%4).. and one half of the tile's 16-column chunks.
+constexpr int kGemmThreads = 256;
+
 template <int BN, int MT, int EPI>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
                 const GemmKernelArgs a) {
   using C = GemmCfg<BN, MT>;
@@ -211,18 +216,22 @@ __global__ void __launch_bounds__(128, 1)
   __syncwarp();
   pdl_wait();  // outputs are written after the previous kernel has completed
 
-  // Epilogue: warp w owns TMEM lanes [32w, 32w+32) = token rows of each tile.
+  // Epilogue: warp w owns TMEM lanes [32(w%4), 32(w%4)+32) = token rows of each
+  // tile, and chunk half w/4 of the tile's columns.
   // tcgen05.ld is warp-collective: the whole warp takes the same branch.
   const bool ok = __all_sync(0xffffffffu, mbar_wait(accum, 0, 0x103));
   tc_fence_after();
   if (ok) {
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const int q4 = warp & 3, hf = warp >> 2;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
 #pragma unroll 1
     for (int mt = 0; mt < MT; ++mt) {
-      const int m = (m_group * MT + mt) * kTileM + warp * 32 + lane;
+      const int m = (m_group * MT + mt) * kTileM + q4 * 32 + lane;
       if (EPI == kEpiSiluMul) {
+        constexpr int kChunks = BN / 32, kHalf = (kChunks + 1) / 2;
+        const int c_lo = hf * kHalf, c_hi = min(kChunks, c_lo + kHalf);
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = c_lo; c < c_hi; ++c) {
           float g[16], u[16];
           tmem_ld16(lane_base + mt * C::kAccStride + c * 16, g);
           tmem_ld16(lane_base + mt * C::kAccStride + BN / 2 + c * 16, u);
@@ -236,11 +245,13 @@ __global__ void __launch_bounds__(128, 1)
           }
         }
       } else {
+        constexpr int kChunks = BN / 16, kHalf = (kChunks + 1) / 2;
+        const int c_lo = hf * kHalf, c_hi = min(kChunks, c_lo + kHalf);
         unsigned long long best = 0;
         int ex0 = 0, ex1 = 0;
         if (EPI == kEpiF32Argmax) { ex0 = a.excl[0]; ex1 = ex0 + a.excl[1]; }
 #pragma unroll 1
-        for (int c = 0; c < BN / 16; ++c) {
+        for (int c = c_lo; c < c_hi; ++c) {
           float v[16];
           tmem_ld16(lane_base + mt * C::kAccStride + c * 16, v);
           const int n0 = n_tile * BN + c * 16;
@@ -359,7 +370,7 @@ static int launch_t(const GemmShape& s, const CUtensorMap& mx, const CUtensorMap
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
     return RB_ERR_CUDA;
   dim3 grid(s.n_tiles, s.splits, s.m_groups);
-  return launch_k(kern, grid, dim3(128), C::kSmemBytes, stream, pdl, mx, mw, ka);
+  return launch_k(kern, grid, dim3(kGemmThreads), C::kSmemBytes, stream, pdl, mx, mw, ka);
 }
 
 template <int BN, int MT>
