@@ -5,6 +5,7 @@
 #include "gemm.cu"
 #include "attention_tc.cu"
 #include "attention.cu"
+#include "attention_noalloc.cu"
 #include "elementwise.cu"
 #include "capi.cu"
 #include "engine.cu"
