@@ -62,6 +62,18 @@ def measured_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def profiled_traffic():
+    """dram__bytes_read.sum + dram__bytes_write.sum of one gate|up GEMM launch, from the
+    committed ncu summary (profiles/gemm_gate_up_config3.md), or None."""
+    p = ROOT / "profiles" / "gemm_gate_up_config3.md"
+    if not p.exists():
+        return None
+    for ln in p.read_text().splitlines():
+        if ln.startswith("traffic_bytes_per_launch:"):
+            return float(ln.split(":", 1)[1])
+    return None
+
+
 def config_block(n):
     return {"workload": "config3: trie verify step, 28-layer 7B-class decoder, prefix 3000, 128-node trie",
             "model": "qwen3-style random-init hidden3584 L28 H28/4 D128 F18944 V152064",
@@ -289,7 +301,7 @@ def run_native(args):
         + NODES * cfg.vocab * 4
     roof = {"bound": "hbm", "kernel": "gemm_kernel<256,1,kEpiStoreBF16> gate|up N=37888 K=3584 M=128, packed weights",
             "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "peak_source": src,
-            "traffic": None, "algorithmic_bytes": gu_bytes, "launch_ms": gu_ms}
+            "traffic": profiled_traffic(), "algorithmic_bytes": gu_bytes, "launch_ms": gu_ms}
     step_roof = {"bound": "hbm", "algorithmic_bytes": step_bytes, "achieved": step_bytes / (ms_step * 1e-3) / 1e9,
                  "peak": hbm, "unit": "GB/s", "frac": step_bytes / (ms_step * 1e-3) / 1e9 / hbm,
                  "floor_ms": step_bytes / (hbm * 1e9) * 1e3}
