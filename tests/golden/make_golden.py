@@ -228,7 +228,8 @@ def main():
     if "kernels" in only:
         gen_kernels(HERE)
     if "model" in only:
-        from tests.golden import make_model_golden
+        sys.path.insert(0, str(HERE))
+        import make_model_golden
         make_model_golden.generate(HERE)
     print("fixtures written to", HERE)
 
