@@ -19,6 +19,14 @@ barrier and the max over ranks is reported.
 
 --impl reference: the reference's CPU path (the numpy oracle restating it,
 oracle/) on the host cores, on a bounded sample of the same step.
+
+--kernel-case gemm_gate_up | attention: only that kernel at its config-3
+shape (--warmup untimed launches, then --steps timed ones), for profiling one
+kernel on a small footprint; prints one JSON line with the per-launch time.
+  gemm_gate_up: the fused gate|up GEMM + SiLU*mul epilogue, 128 rows,
+                two layers' packed weights (0.54 GB) used alternately.
+  attention:    one layer's trie attention, 28/4 heads, 3000-key prefix,
+                128-node trie, bf16.
 """
 from __future__ import annotations
 
@@ -51,6 +59,7 @@ def parse():
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-case", default=None, choices=["gemm_gate_up", "attention"])
     return ap.parse_args()
 
 
@@ -198,7 +207,7 @@ def run_native(args):
     from respect_b200.candidates.trie import build_trie
     from respect_b200.decoding.acceptance import walk
     from respect_b200.decoding.engine import DecoderConfig, DecoderWeights, VerifyEngine
-    from respect_b200.kernels.gemm import linear_packed
+    from respect_b200.kernels.gemm import linear_swiglu_packed
 
     cfg = DecoderConfig.baseline_7b()
     w = DecoderWeights.random(cfg, dev, seed=0)
@@ -273,20 +282,20 @@ def run_native(args):
     e2e = {"value": world * committed * k2 / (ms2 / 1e3), "unit": "committed tokens/s",
            "ms_per_step": ms2 / k2, "h2d_bytes_per_step": 32 + 3 * 4 * NODES, "d2h_bytes_per_step": 8 * NODES}
 
-    # roofline of the dominant kernel: the gate|up weight-streaming GEMM of a layer
+    # roofline of the dominant kernel: the fused gate|up + SiLU*mul GEMM of a layer
     hbm, tf, src = measured_peaks()
     xg = torch.randn(NODES, cfg.hidden, device=dev, generator=torch.Generator(device=dev).manual_seed(5)).to(torch.bfloat16)
     ngu = 2 * cfg.ffn
     bufs = [pk["wgu"] for pk in eng.packed]   # the engine's packed gate|up weights, one per layer
     for _ in range(3):
-        linear_packed(xg, bufs[0], ngu)
+        linear_swiglu_packed(xg, bufs[0], cfg.ffn)
     reps = 56
     # captured in a CUDA graph so that host launch overhead does not enter the timing;
     # layers rotate so every launch streams its weights from HBM
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         for i in range(reps):
-            linear_packed(xg, bufs[i % len(bufs)], ngu)
+            linear_swiglu_packed(xg, bufs[i % len(bufs)], cfg.ffn)
     g.replay()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -295,11 +304,11 @@ def run_native(args):
     e1.record(st)
     torch.cuda.synchronize()
     gu_ms = e0.elapsed_time(e1) / reps
-    gu_bytes = ngu * cfg.hidden * 2 + xg.numel() * 2 + NODES * ngu * 2
+    gu_bytes = ngu * cfg.hidden * 2 + xg.numel() * 2 + NODES * cfg.ffn * 2
     achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
     step_bytes = cfg.weight_bytes_per_step() + 2 * cfg.n_layers * 2 * cfg.n_kv_heads * (PROMPT + NODES) * 128 \
         + NODES * cfg.vocab * 4
-    roof = {"bound": "hbm", "kernel": "gemm_kernel<256,1,kEpiStoreBF16> gate|up N=37888 K=3584 M=128, packed weights",
+    roof = {"bound": "hbm", "kernel": "gemm_kernel<256,1,kEpiSiluMul> fused gate|up+SiLU*mul N=37888 K=3584 M=128",
             "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "peak_source": src,
             "traffic": profiled_traffic(), "algorithmic_bytes": gu_bytes, "launch_ms": gu_ms}
     step_roof = {"bound": "hbm", "algorithmic_bytes": step_bytes, "achieved": step_bytes / (ms_step * 1e-3) / 1e9,
@@ -326,9 +335,63 @@ def run_native(args):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------ single-kernel cases
+def run_kernel_case(args):
+    import torch
+    from respect_b200.decoding.engine import DecoderConfig
+    dev = torch.device("cuda", 0)
+    cfg = DecoderConfig.baseline_7b()
+    g = torch.Generator(device=dev).manual_seed(7)
+    st = torch.cuda.current_stream(dev)
+    if args.kernel_case == "gemm_gate_up":
+        from respect_b200.kernels.gemm import linear_swiglu_packed, pack_gate_up
+        h, F = cfg.hidden, cfg.ffn
+        ws = []
+        for _ in range(2):
+            wg = (torch.randn(F, h, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            wu = (torch.randn(F, h, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            ws.append(pack_gate_up(wg, wu))
+            del wg, wu
+        x = torch.randn(NODES, h, device=dev, generator=g).to(torch.bfloat16)
+
+        def launch(i):
+            linear_swiglu_packed(x, ws[i % 2], F)
+        algo = 2 * F * h * 2 + NODES * h * 2 + NODES * F * 2
+    else:
+        from respect_b200.kernels.attention import fused_attn_hyb
+        from oracle.trie import ancestry
+        H, HK, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        q = (torch.randn(H, NODES, D, device=dev, generator=g) / D ** 0.5).to(torch.bfloat16)
+        kc = torch.randn(HK, PROMPT + 1024, D, device=dev, generator=g).to(torch.bfloat16)
+        vc = torch.randn(HK, PROMPT + 1024, D, device=dev, generator=g).to(torch.bfloat16)
+        rng = np.random.default_rng(3)
+        parents = [-1] + [int(rng.integers(0, i)) for i in range(1, NODES)]
+        msk = torch.from_numpy(ancestry(parents)).to(dev)
+        kp, vp = kc[:, :PROMPT], vc[:, :PROMPT]
+        kn, vn = kc[:, PROMPT:PROMPT + NODES], vc[:, PROMPT:PROMPT + NODES]
+
+        def launch(i):
+            fused_attn_hyb(q, kp, vp, kn, vn, msk)
+        algo = 2 * HK * (PROMPT + NODES) * D * 2 + 2 * H * NODES * D * 2
+    for i in range(args.warmup):
+        launch(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(args.steps):
+        launch(i)
+    e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    print(json.dumps({"kernel_case": args.kernel_case, "launches": args.steps, "us_per_launch": us,
+                      "algorithmic_bytes": algo, "GBps": algo / (us * 1e-6) / 1e9}), flush=True)
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.kernel_case:
+        run_kernel_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_native(args)

@@ -14,6 +14,7 @@
  *   rb_rmsnorm          respect/kernels/rmsnorm.py:25-32     rmsnorm
  *   rb_rope             respect/system/fused.py:67-75        rope
  *   rb_silu_mul         respect/system/fused.py:116-123      silu_mul
+ *   rb_linear_swiglu_packed  fused.py:106-123 silu_mul fused into the gate|up linear (patch.py:26-37)
  *   rb_greedy_token     respect/decoding/acceptance.py:11-23 mask_action_vocab + greedy_token
  *   rb_compact_kv       respect/decoding/kv_buffer.py:93-104 compact
  *   rb_trie_node_mask   respect/candidates/trie.py:51-64 + respect/kernels/dispatch.py:94-115
@@ -131,6 +132,21 @@ RB_API size_t rb_linear_packed_bytes(int N, int K, int BN);
 RB_API int rb_pack_linear_weight(const void* w, int64_t ldw, int N, int K, int BN, void* out, void* stream);
 RB_API int rb_linear_packed(const void* x, int64_t ldx, const void* w_packed, void* out, int64_t ldo,
                             int out_dtype, int M, int N, int K, void* workspace, size_t ws_bytes, void* stream);
+
+/* Fused SwiGLU projection: out[M, F] = silu(x Wg^T) * (x Wu^T), bf16, the HF MLP's
+ * act_fn(gate_proj(x)) * up_proj(x) with its rounding points (each projection
+ * rounded to bf16, silu rounded, product rounded; respect/system/fused.py:106-123
+ * on top of the dedicated linears of respect/kernels/patch.py:26-37), in one
+ * launch: the SiLU*mul runs in the GEMM epilogue, the two projections never
+ * reach HBM. w_gu is Wg and Wu [F, K] interleaved in 128-row blocks (rows
+ * 256i..256i+127 = Wg rows 128i.., rows 256i+128.. = Wu rows 128i..), packed by
+ * rb_pack_linear_weight(N = 2F, BN = 256). One K split at every shape, so a
+ * row's result does not depend on M; where rb_linear's own plan for (2F, K) is
+ * also one split of 256-wide tiles (F = 18944, K = 3584, for one), it is bitwise
+ * equal to rb_linear_packed on that weight followed by rb_silu_mul on the two
+ * halves. F % 128 == 0; no workspace. */
+RB_API int rb_linear_swiglu_packed(const void* x, int64_t ldx, const void* w_gu, void* out, int64_t ldo, int M,
+                                   int F, int K, void* stream);
 
 /* ------------------------------------------------------------------ rmsnorm
  * y = w * to_dtype(x * rsqrt(mean(x^2) + eps)), one row per block, fixed

@@ -65,6 +65,8 @@ SIGNATURES = {
     "rb_pack_linear_weight": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p]),
     "rb_linear_packed": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_int,
                                  c_void_p, c_size_t, c_void_p]),
+    "rb_linear_swiglu_packed": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int, c_int, c_int,
+                                        c_void_p]),
     "rb_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_int, c_int, c_void_p]),
     "rb_rope": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                         c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),

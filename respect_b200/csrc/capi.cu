@@ -83,6 +83,24 @@ int rb_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, void* out,
   return splitk_reduce(a.partial, s.splits, M, N, out, ldo, out_dtype == RB_F32, st);
 }
 
+int rb_linear_swiglu_packed(const void* x, int64_t ldx, const void* w_gu, void* out, int64_t ldo, int M, int F,
+                            int K, void* stream) {
+  if (M < 0 || F <= 0 || K <= 0 || !x || !w_gu || !out) return RB_ERR_INVALID_ARG;
+  if (M == 0) return RB_OK;
+  if (F % 128 != 0 || K % 8 != 0 || ldx % 8 != 0 || ldx < K || ldo < F || ldo % 8 != 0) return RB_ERR_UNSUPPORTED;
+  if (!aligned16(x) || !aligned16(w_gu) || !aligned16(out)) return RB_ERR_UNSUPPORTED;
+  const GemmShape s = gemm_plan(M, 2 * F, K, device_sm_count(), 256, 1);
+  CUtensorMap mx, mw;
+  int r = gemm_encode_x(&mx, x, M, K, ldx);
+  if (r != RB_OK) return r;
+  r = gemm_encode_w_packed(&mw, w_gu, 2 * F, K, 256);
+  if (r != RB_OK) return r;
+  GemmLaunch a{};
+  a.x = x; a.ldx = ldx; a.w = w_gu; a.out = out; a.ldo = ldo; a.w_tiled = 1;
+  a.epi = kEpiSiluMul;
+  return gemm_launch_maps(s, mx, mw, a, as_stream(stream));
+}
+
 int rb_linear_bn(int N, int K) {
   if (N <= 0 || K <= 0) return 0;
   return gemm_plan(1, N, K, device_sm_count()).BN;

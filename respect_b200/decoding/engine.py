@@ -139,8 +139,8 @@ class DecoderWeights:
     @staticmethod
     def pack_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
         """[ffn, hidden] x 2 -> [2 ffn, hidden] in 128-row gate|up blocks."""
-        f, h = gate.shape
-        return torch.stack([gate.view(f // 128, 128, h), up.view(f // 128, 128, h)], dim=1).reshape(2 * f, h)
+        from respect_b200.kernels.gemm import interleave_gate_up
+        return interleave_gate_up(gate, up)
 
     @staticmethod
     def unpack_gate_up(wgu: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

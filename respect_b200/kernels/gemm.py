@@ -57,3 +57,30 @@ def linear_packed(x, w_packed, N, out_dtype=None):
     _lib.call("rb_linear_packed", xs.data_ptr(), xs.stride(0), w_packed.data_ptr(), out.data_ptr(), out.stride(0),
               _lib.dtype_code(od), M, N, K, ws.data_ptr() if ws is not None else None, nbytes, _lib.stream_of(xs))
     return out.reshape(*x.shape[:-1], N)
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """Gate and up weights [F, K] -> [2F, K] in alternating 128-row blocks (gate, up, gate, ...)."""
+    f, k = gate.shape
+    if f % 128 != 0 or up.shape != gate.shape:
+        raise ValueError("gate/up weights must share a shape with a multiple of 128 rows")
+    return torch.stack([gate.reshape(f // 128, 128, k), up.reshape(f // 128, 128, k)], dim=1).reshape(2 * f, k)
+
+
+def pack_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """The packed weight linear_swiglu_packed reads (interleaved, then packed with BN = 256)."""
+    return pack_weight(interleave_gate_up(gate, up), bn=256)
+
+
+def linear_swiglu_packed(x, w_gu_packed, F):
+    """silu(x @ gate^T) * (x @ up^T) -> (..., F) bf16 in one launch (rb_linear_swiglu_packed);
+    bitwise equal to silu_mul(linear(x, gate), linear(x, up)) computed on the interleaved weight."""
+    K = x.shape[-1]
+    xs = x.reshape(-1, K).contiguous()
+    if xs.dtype != torch.bfloat16 or w_gu_packed.dtype != torch.bfloat16:
+        raise TypeError("respect_b200.linear_swiglu_packed takes bf16 x and weights")
+    M = xs.shape[0]
+    out = torch.empty((M, F), device=x.device, dtype=torch.bfloat16)
+    _lib.call("rb_linear_swiglu_packed", xs.data_ptr(), xs.stride(0), w_gu_packed.data_ptr(), out.data_ptr(),
+              out.stride(0), M, F, K, _lib.stream_of(xs))
+    return out.reshape(*x.shape[:-1], F)

@@ -180,6 +180,41 @@ def test_linear_packed_is_bitwise_linear(M, N, K):
         assert torch.equal(linear_packed(x, wp, N, out_dtype=od), linear(x, w, out_dtype=od))
 
 
+@pytest.mark.parametrize("M,F,K", [(128, 18944, 3584), (1, 18944, 3584), (200, 1024, 512), (5, 384, 200)])
+def test_linear_swiglu_packed(M, F, K):
+    """Fused gate|up + SiLU*mul: equals eager silu(gate)*up on the same bf16 projections, row-invariant,
+    and (7B shape: one split of 256-wide tiles in rb_linear's own plan) bitwise the unfused composition."""
+    from respect_b200 import _lib
+    from respect_b200.kernels.gemm import (interleave_gate_up, linear, linear_packed, linear_swiglu_packed,
+                                           pack_gate_up)
+    g = torch.Generator(device=DEV).manual_seed(F + K)
+    x = torch.randn(max(M, 2), K, device=DEV, generator=g).to(torch.bfloat16)[:M]
+    wg = (torch.randn(F, K, device=DEV, generator=g) * 0.05).to(torch.bfloat16)
+    wu = (torch.randn(F, K, device=DEV, generator=g) * 0.05).to(torch.bfloat16)
+    wp = pack_gate_up(wg, wu)
+    y = linear_swiglu_packed(x, wp, F)
+    assert y.shape == (M, F) and y.dtype == torch.bfloat16
+    # row invariance: each row alone gives the same bits
+    for r in sorted({0, M // 2, M - 1}):
+        assert torch.equal(linear_swiglu_packed(x[r:r + 1], wp, F), y[r:r + 1])
+    # against fp64 projections rounded to bf16. A K-long fp32 sum that lands next to a bf16
+    # midpoint rounds the other way (one ulp, <= 2^-7 relative, ~0.1% of elements); through
+    # silu (gain <= 1.1 for g > 0) and the two later roundings that is up to ~2^-5 relative.
+    gr = (x.double() @ wg.double().T).to(torch.bfloat16)
+    ur = (x.double() @ wu.double().T).to(torch.bfloat16)
+    ref = (torch.nn.functional.silu(gr) * ur).float()
+    assert torch.all((y.float() - ref).abs() <= ref.abs() * 2 ** -5 + 1e-4 * ref.abs().max())
+    assert (y.float() != ref).float().mean() < 0.01
+    N, plan_bn = 2 * F, _lib.lib().rb_linear_bn(2 * F, K)
+    if (F, K) == (18944, 3584):
+        assert plan_bn == 256
+        gu = linear_packed(x, pack_gate_up(wg, wu), N).view(M, F // 128, 2, 128)
+        from respect_b200.system.fused import silu_mul
+        comp = silu_mul(gu[:, :, 0].reshape(M, F).contiguous(), gu[:, :, 1].reshape(M, F).contiguous())
+        assert torch.equal(y, comp)
+        assert torch.equal(linear(x, interleave_gate_up(wg, wu)), gu.reshape(M, N))
+
+
 # ---------------------------------------------------------------- rmsnorm / rope / silu
 @pytest.mark.parametrize("N", [128, 384, 3584, 4096])
 def test_rmsnorm_vs_oracle_and_row_invariance(N):
