@@ -6,12 +6,14 @@ load, every operator raises. There is no CPU or library fallback.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "librespect_b200.so"
+# RESPECT_B200_LIB names a librespect_b200.so built elsewhere (e.g. with other compile-time options).
+LIB_PATH = Path(os.environ.get("RESPECT_B200_LIB") or Path(__file__).resolve().parent / "librespect_b200.so")
 
 RB_OK = 0
 RB_F32, RB_BF16, RB_U8, RB_I32, RB_I64 = 0, 1, 2, 3, 4

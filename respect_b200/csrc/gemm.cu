@@ -2,6 +2,7 @@
 // Follows the contract of respect/kernels/gemm.py:11-41: fixed K order, fp32
 // accumulation, bf16 or fp32 output, bias handled by the caller.
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -51,6 +52,7 @@ struct GemmKernelArgs {
   float* partial;
   unsigned long long* keys;
   const int* excl;
+  int tma_out;  // epilogue stages the tile in shared memory and writes it with TMA stores (tmo)
 };
 
 template <int EPI>
@@ -117,7 +119,7 @@ constexpr int kGemmThreads = 256;
 template <int BN, int MT, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
-                const GemmKernelArgs a) {
+                const __grid_constant__ CUtensorMap tmo, const GemmKernelArgs a) {
   using C = GemmCfg<BN, MT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -141,6 +143,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmx);
     tma_prefetch_desc(&tmw);
+    if (a.tma_out) tma_prefetch_desc(&tmo);
     for (int s = 0; s < C::kWStages; ++s) {
       mbar_init(wfull0 + 8 * s, 1);
       mbar_init(wempty0 + 8 * s, 1);
@@ -219,9 +222,78 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // Epilogue: warp w owns TMEM lanes [32(w%4), 32(w%4)+32) = token rows of each
   // tile, and chunk half w/4 of the tile's columns.
   // tcgen05.ld is warp-collective: the whole warp takes the same branch.
-  const bool ok = __all_sync(0xffffffffu, mbar_wait(accum, 0, 0x103));
+  // One verdict for the whole CTA (the staged epilogue below has block barriers).
+  const bool ok = __syncthreads_and(mbar_wait(accum, 0, 0x103)) != 0;
   tc_fence_after();
-  if (ok) {
+  constexpr bool kSilu = EPI == kEpiSiluMul;
+  constexpr int kOutCols = kSilu ? BN / 2 : BN;  // output columns of one tile
+  constexpr int kBoxCols = kSilu ? 64 : 32;       // 128-byte rows in a staged box
+  constexpr bool kCanStage = (EPI == kEpiPartial || kSilu) && kOutCols % kBoxCols == 0;
+  if constexpr (kCanStage) {
+    if (ok && a.tma_out) {
+      // Staged epilogue: the tile goes to shared memory (the weight ring, idle
+      // once the accumulator is final) as 128 x 128-byte boxes in the 128-byte
+      // swizzle (16-byte piece j of row r at piece j ^ (r & 7)), then one thread
+      // writes the boxes with TMA tiled stores: whole lines instead of each
+      // thread storing its own row in 16-byte pieces. Rows >= M are clipped by
+      // the tensor map.
+      constexpr int kBoxes = kOutCols / kBoxCols;
+      constexpr int kBoxBytes = kTileM * 128;
+      static_assert(kBoxes * kBoxBytes <= C::kWStages * C::kWTileBytes, "staging fits in the weight ring");
+      uint8_t* stage = smem + C::kWOff;
+      const int q4 = warp & 3, hf = warp >> 2;
+      const int r = q4 * 32 + lane;
+      const uint32_t lane_base = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+      uint8_t* srow = stage + r * 128;
+#pragma unroll 1
+      for (int mt = 0; mt < MT; ++mt) {
+        constexpr int kChunks = kOutCols / 16, kHalf = kChunks / 2;
+#pragma unroll 1
+        for (int c = hf * kHalf; c < (hf + 1) * kHalf; ++c) {
+          if constexpr (kSilu) {
+            float g[16], u[16];
+            tmem_ld16(lane_base + mt * C::kAccStride + c * 16, g);
+            tmem_ld16(lane_base + mt * C::kAccStride + BN / 2 + c * 16, u);
+            uint32_t w[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(silu_mul_bf16(g[2 * i], u[2 * i]),
+                                                           silu_mul_bf16(g[2 * i + 1], u[2 * i + 1]));
+            uint8_t* box = srow + (c >> 2) * kBoxBytes;
+            const int j0 = (c & 3) * 2;
+            *reinterpret_cast<uint4*>(box + (((j0) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4*>(box + (((j0 + 1) ^ (r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+          } else {
+            float v[16];
+            tmem_ld16(lane_base + mt * C::kAccStride + c * 16, v);
+            uint8_t* box = srow + (c >> 1) * kBoxBytes;
+            const int j0 = (c & 1) * 4;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              *reinterpret_cast<float4*>(box + (((j0 + i) ^ (r & 7)) << 4)) =
+                  make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          }
+        }
+        fence_proxy_async_smem();  // generic-proxy stores -> visible to the TMA engine
+        __syncthreads();
+        const int row0 = (m_group * MT + mt) * kTileM;
+        if (threadIdx.x == 0 && row0 < a.M) {
+          const int out_n = kSilu ? a.N / 2 : a.N;  // boxes start inside the tensor; the tail is clipped
+#pragma unroll 1
+          for (int b = 0; b < kBoxes; ++b) {
+            const int x = n_tile * kOutCols + b * kBoxCols;
+            if (x >= out_n) break;
+            const uint32_t src = smem_u32(stage + b * kBoxBytes);
+            if constexpr (kSilu) tma_store_2d(&tmo, src, x, row0);
+            else tma_store_3d(&tmo, src, x, row0, split);
+          }
+          bulk_commit();
+          bulk_wait_all();  // shared memory read and global writes performed
+        }
+        __syncthreads();  // the staging tile may be refilled / the CTA may exit
+      }
+    }
+  }
+  if (ok && !(kCanStage && a.tma_out)) {
     const int q4 = warp & 3, hf = warp >> 2;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
 #pragma unroll 1
@@ -363,25 +435,25 @@ int gemm_pack_weight(const void* w, int64_t ldw, int N, int K, int BN, void* out
 }
 
 template <int BN, int MT, int EPI>
-static int launch_t(const GemmShape& s, const CUtensorMap& mx, const CUtensorMap& mw,
+static int launch_t(const GemmShape& s, const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& mo,
                     const GemmKernelArgs& ka, cudaStream_t stream, bool pdl) {
   using C = GemmCfg<BN, MT>;
   auto kern = gemm_kernel<BN, MT, EPI>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
     return RB_ERR_CUDA;
   dim3 grid(s.n_tiles, s.splits, s.m_groups);
-  return launch_k(kern, grid, dim3(kGemmThreads), C::kSmemBytes, stream, pdl, mx, mw, ka);
+  return launch_k(kern, grid, dim3(kGemmThreads), C::kSmemBytes, stream, pdl, mx, mw, mo, ka);
 }
 
 template <int BN, int MT>
-static int launch_epi(const GemmShape& s, const CUtensorMap& mx, const CUtensorMap& mw,
+static int launch_epi(const GemmShape& s, const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& mo,
                       const GemmKernelArgs& ka, int epi, cudaStream_t stream, bool pdl) {
   switch (epi) {
-    case kEpiStoreBF16: return launch_t<BN, MT, kEpiStoreBF16>(s, mx, mw, ka, stream, pdl);
-    case kEpiStoreF32: return launch_t<BN, MT, kEpiStoreF32>(s, mx, mw, ka, stream, pdl);
-    case kEpiSiluMul: return launch_t<BN, MT, kEpiSiluMul>(s, mx, mw, ka, stream, pdl);
-    case kEpiPartial: return launch_t<BN, MT, kEpiPartial>(s, mx, mw, ka, stream, pdl);
-    case kEpiF32Argmax: return launch_t<BN, MT, kEpiF32Argmax>(s, mx, mw, ka, stream, pdl);
+    case kEpiStoreBF16: return launch_t<BN, MT, kEpiStoreBF16>(s, mx, mw, mo, ka, stream, pdl);
+    case kEpiStoreF32: return launch_t<BN, MT, kEpiStoreF32>(s, mx, mw, mo, ka, stream, pdl);
+    case kEpiSiluMul: return launch_t<BN, MT, kEpiSiluMul>(s, mx, mw, mo, ka, stream, pdl);
+    case kEpiPartial: return launch_t<BN, MT, kEpiPartial>(s, mx, mw, mo, ka, stream, pdl);
+    case kEpiF32Argmax: return launch_t<BN, MT, kEpiF32Argmax>(s, mx, mw, mo, ka, stream, pdl);
   }
   return RB_ERR_INVALID_ARG;
 }
@@ -403,14 +475,29 @@ int gemm_launch_maps(const GemmShape& s, const CUtensorMap& mx, const CUtensorMa
   if (a.epi == kEpiF32Argmax && (!a.keys || !a.excl)) return RB_ERR_INVALID_ARG;
   if (a.epi != kEpiPartial && s.splits != 1) return RB_ERR_INVALID_ARG;
   if (a.epi == kEpiSiluMul && (s.N % s.BN) != 0) return RB_ERR_UNSUPPORTED;
+  // Output tensor map for the staged (TMA store) epilogue where the layout allows it.
+  CUtensorMap mo;
+  memset(&mo, 0, sizeof(mo));
+  ka.tma_out = 0;
+  if (a.epi == kEpiPartial && s.BN % 32 == 0 && s.N % 4 == 0 && aligned16(a.partial)) {
+    const uint64_t dims[3] = {static_cast<uint64_t>(s.N), static_cast<uint64_t>(s.M),
+                              static_cast<uint64_t>(s.splits)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(s.N) * 4, static_cast<uint64_t>(s.M) * s.N * 4};
+    const uint32_t box[3] = {32, kTileM, 1};
+    ka.tma_out = encode_tiled(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, a.partial, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_128B) == RB_OK;
+  } else if (a.epi == kEpiSiluMul && (s.BN / 2) % 64 == 0 && a.ldo % 8 == 0 && aligned16(a.out)) {
+    ka.tma_out = encode_2d_bf16(&mo, a.out, static_cast<uint64_t>(s.N / 2), static_cast<uint64_t>(s.M), a.ldo,
+                                64, kTileM) == RB_OK;
+  }
   const int key = s.BN * 4 + s.mt;
   switch (key) {
-    case 256 * 4 + 1: return launch_epi<256, 1>(s, mx, mw, ka, a.epi, stream, pdl);
-    case 256 * 4 + 2: return launch_epi<256, 2>(s, mx, mw, ka, a.epi, stream, pdl);
-    case 208 * 4 + 1: return launch_epi<208, 1>(s, mx, mw, ka, a.epi, stream, pdl);
-    case 208 * 4 + 2: return launch_epi<208, 2>(s, mx, mw, ka, a.epi, stream, pdl);
-    case 128 * 4 + 1: return launch_epi<128, 1>(s, mx, mw, ka, a.epi, stream, pdl);
-    case 128 * 4 + 2: return launch_epi<128, 2>(s, mx, mw, ka, a.epi, stream, pdl);
+    case 256 * 4 + 1: return launch_epi<256, 1>(s, mx, mw, mo, ka, a.epi, stream, pdl);
+    case 256 * 4 + 2: return launch_epi<256, 2>(s, mx, mw, mo, ka, a.epi, stream, pdl);
+    case 208 * 4 + 1: return launch_epi<208, 1>(s, mx, mw, mo, ka, a.epi, stream, pdl);
+    case 208 * 4 + 2: return launch_epi<208, 2>(s, mx, mw, mo, ka, a.epi, stream, pdl);
+    case 128 * 4 + 1: return launch_epi<128, 1>(s, mx, mw, mo, ka, a.epi, stream, pdl);
+    case 128 * 4 + 2: return launch_epi<128, 2>(s, mx, mw, mo, ka, a.epi, stream, pdl);
   }
   return RB_ERR_UNSUPPORTED;
 }
