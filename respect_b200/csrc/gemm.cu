@@ -42,6 +42,23 @@ struct GemmCfg {
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
 };
 
+// Output element size of an epilogue, and the row width in bytes of the
+// shared-memory boxes the staged epilogue writes with TMA (0: not staged):
+// 128-byte rows where a tile's output is a whole number of them, else 64.
+// Staged: the split-K partials and the bf16 outputs, whose single-wave grids
+// finish on their last CTA's stores. The fp32 outputs (the many-wave vocabulary
+// projection) keep the direct per-thread stores, which the CTA does not wait
+// for before it exits (measured: staging made the lm_head 4% slower).
+__host__ __device__ constexpr int gemm_out_elem_bytes(int epi) {
+  return (epi == kEpiStoreBF16 || epi == kEpiSiluMul) ? 2 : 4;
+}
+__host__ __device__ constexpr int gemm_stage_row_bytes(int epi, int bn) {
+  return (epi == kEpiStoreF32 || epi == kEpiF32Argmax) ? 0
+         : ((epi == kEpiSiluMul ? bn / 2 : bn) * gemm_out_elem_bytes(epi)) % 128 == 0 ? 128
+         : ((epi == kEpiSiluMul ? bn / 2 : bn) * gemm_out_elem_bytes(epi)) % 64 == 0 ? 64
+                                                                                     : 0;
+}
+
 struct GemmKernelArgs {
   int M, N, K;
   int k_chunks, splits;
@@ -227,52 +244,79 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   constexpr bool kSilu = EPI == kEpiSiluMul;
   constexpr int kOutCols = kSilu ? BN / 2 : BN;  // output columns of one tile
-  constexpr int kBoxCols = kSilu ? 64 : 32;       // 128-byte rows in a staged box
-  constexpr bool kCanStage = (EPI == kEpiPartial || kSilu) && kOutCols % kBoxCols == 0;
+  constexpr int kRowBytes = gemm_stage_row_bytes(EPI, BN);  // staged box row: 128 or 64 bytes (0: not staged)
+  constexpr bool kCanStage = kRowBytes > 0;
   if constexpr (kCanStage) {
     if (ok && a.tma_out) {
       // Staged epilogue: the tile goes to shared memory (the weight ring, idle
-      // once the accumulator is final) as 128 x 128-byte boxes in the 128-byte
-      // swizzle (16-byte piece j of row r at piece j ^ (r & 7)), then one thread
-      // writes the boxes with TMA tiled stores: whole lines instead of each
-      // thread storing its own row in 16-byte pieces. Rows >= M are clipped by
-      // the tensor map.
+      // once the accumulator is final) as boxes of 128 rows x kRowBytes in the
+      // matching TMA swizzle (16-byte piece j of row r at j ^ (r & 7) for
+      // 128-byte rows, j ^ ((r >> 1) & 3) for 64-byte rows), then one thread
+      // writes the boxes with TMA tiled stores: whole lines instead of every
+      // thread storing its own row in 16-byte pieces. Rows >= M and columns
+      // >= N are clipped by the tensor map.
+      constexpr int kElem = gemm_out_elem_bytes(EPI);
+      constexpr int kBoxCols = kRowBytes / kElem;
       constexpr int kBoxes = kOutCols / kBoxCols;
-      constexpr int kBoxBytes = kTileM * 128;
+      constexpr int kBoxBytes = kTileM * kRowBytes;
+      constexpr int kPieces = 16 * kElem / 16;  // 16-byte pieces per 16-column chunk
       static_assert(kBoxes * kBoxBytes <= C::kWStages * C::kWTileBytes, "staging fits in the weight ring");
       uint8_t* stage = smem + C::kWOff;
       const int q4 = warp & 3, hf = warp >> 2;
       const int r = q4 * 32 + lane;
+      const int sw = kRowBytes == 128 ? (r & 7) : ((r >> 1) & 3);
       const uint32_t lane_base = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
-      uint8_t* srow = stage + r * 128;
+      uint8_t* srow = stage + r * kRowBytes;
+      constexpr int kChunks = kOutCols / 16, kHalfC = (kChunks + 1) / 2;
+      const int c_lo = hf * kHalfC, c_hi = min(kChunks, c_lo + kHalfC);
 #pragma unroll 1
       for (int mt = 0; mt < MT; ++mt) {
-        constexpr int kChunks = kOutCols / 16, kHalf = kChunks / 2;
+        const int m = (m_group * MT + mt) * kTileM + r;
+        unsigned long long best = 0;
+        int ex0 = 0, ex1 = 0;
+        if (EPI == kEpiF32Argmax) { ex0 = a.excl[0]; ex1 = ex0 + a.excl[1]; }
 #pragma unroll 1
-        for (int c = hf * kHalf; c < (hf + 1) * kHalf; ++c) {
+        for (int c = c_lo; c < c_hi; ++c) {
+          uint32_t w[16 * kElem / 4];
           if constexpr (kSilu) {
             float g[16], u[16];
             tmem_ld16(lane_base + mt * C::kAccStride + c * 16, g);
             tmem_ld16(lane_base + mt * C::kAccStride + BN / 2 + c * 16, u);
-            uint32_t w[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(silu_mul_bf16(g[2 * i], u[2 * i]),
-                                                           silu_mul_bf16(g[2 * i + 1], u[2 * i + 1]));
-            uint8_t* box = srow + (c >> 2) * kBoxBytes;
-            const int j0 = (c & 3) * 2;
-            *reinterpret_cast<uint4*>(box + (((j0) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-            *reinterpret_cast<uint4*>(box + (((j0 + 1) ^ (r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+            for (int i = 0; i < 8; ++i)
+              w[i] = pack_bf16x2(silu_mul_bf16(g[2 * i], u[2 * i]), silu_mul_bf16(g[2 * i + 1], u[2 * i + 1]));
           } else {
             float v[16];
             tmem_ld16(lane_base + mt * C::kAccStride + c * 16, v);
-            uint8_t* box = srow + (c >> 1) * kBoxBytes;
-            const int j0 = (c & 1) * 4;
+            if constexpr (kElem == 2) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              *reinterpret_cast<float4*>(box + (((j0 + i) ^ (r & 7)) << 4)) =
-                  make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+              for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(v[i]);
+            }
+            if constexpr (EPI == kEpiF32Argmax) {
+              const int n0 = n_tile * BN + c * 16;
+              if (m < a.M) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const int n = n0 + i;
+                  if (n < a.N && (n < ex0 || n >= ex1)) {
+                    const unsigned long long k = argmax_key(v[i], n);
+                    best = k > best ? k : best;
+                  }
+                }
+              }
+            }
           }
+          const int col_bytes = (c * 16 % kBoxCols) * kElem;
+          uint8_t* box = srow + (c * 16 / kBoxCols) * kBoxBytes;
+#pragma unroll
+          for (int i = 0; i < kPieces; ++i)
+            *reinterpret_cast<uint4*>(box + (((col_bytes >> 4) + i) ^ sw) * 16) =
+                make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         }
+        if (EPI == kEpiF32Argmax && m < a.M && best != 0) atomicMax(a.keys + m, best);
         fence_proxy_async_smem();  // generic-proxy stores -> visible to the TMA engine
         __syncthreads();
         const int row0 = (m_group * MT + mt) * kTileM;
@@ -283,11 +327,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int x = n_tile * kOutCols + b * kBoxCols;
             if (x >= out_n) break;
             const uint32_t src = smem_u32(stage + b * kBoxBytes);
-            if constexpr (kSilu) tma_store_2d(&tmo, src, x, row0);
-            else tma_store_3d(&tmo, src, x, row0, split);
+            if constexpr (EPI == kEpiPartial) tma_store_3d(&tmo, src, x, row0, split);
+            else tma_store_2d(&tmo, src, x, row0);
           }
           bulk_commit();
-          bulk_wait_all();  // shared memory read and global writes performed
+          bulk_wait_read();  // the staging tile has been read
         }
         __syncthreads();  // the staging tile may be refilled / the CTA may exit
       }
@@ -479,16 +523,27 @@ int gemm_launch_maps(const GemmShape& s, const CUtensorMap& mx, const CUtensorMa
   CUtensorMap mo;
   memset(&mo, 0, sizeof(mo));
   ka.tma_out = 0;
-  if (a.epi == kEpiPartial && s.BN % 32 == 0 && s.N % 4 == 0 && aligned16(a.partial)) {
-    const uint64_t dims[3] = {static_cast<uint64_t>(s.N), static_cast<uint64_t>(s.M),
-                              static_cast<uint64_t>(s.splits)};
-    const uint64_t strides[2] = {static_cast<uint64_t>(s.N) * 4, static_cast<uint64_t>(s.M) * s.N * 4};
-    const uint32_t box[3] = {32, kTileM, 1};
-    ka.tma_out = encode_tiled(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, a.partial, dims, strides, box,
-                              CU_TENSOR_MAP_SWIZZLE_128B) == RB_OK;
-  } else if (a.epi == kEpiSiluMul && (s.BN / 2) % 64 == 0 && a.ldo % 8 == 0 && aligned16(a.out)) {
-    ka.tma_out = encode_2d_bf16(&mo, a.out, static_cast<uint64_t>(s.N / 2), static_cast<uint64_t>(s.M), a.ldo,
-                                64, kTileM) == RB_OK;
+  const int row_bytes = gemm_stage_row_bytes(a.epi, s.BN);
+  const int elem = gemm_out_elem_bytes(a.epi);
+  const CUtensorMapSwizzle swz = row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUtensorMapDataType dt = elem == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const uint32_t box_cols = row_bytes > 0 ? static_cast<uint32_t>(row_bytes / elem) : 0;
+  if (row_bytes > 0 && a.epi == kEpiPartial) {
+    if (s.N % 4 == 0 && aligned16(a.partial)) {
+      const uint64_t dims[3] = {static_cast<uint64_t>(s.N), static_cast<uint64_t>(s.M),
+                                static_cast<uint64_t>(s.splits)};
+      const uint64_t strides[2] = {static_cast<uint64_t>(s.N) * 4, static_cast<uint64_t>(s.M) * s.N * 4};
+      const uint32_t box[3] = {box_cols, kTileM, 1};
+      ka.tma_out = encode_tiled(&mo, dt, 3, a.partial, dims, strides, box, swz) == RB_OK;
+    }
+  } else if (row_bytes > 0) {
+    const int out_n = a.epi == kEpiSiluMul ? s.N / 2 : s.N;
+    if ((a.ldo * elem) % 16 == 0 && aligned16(a.out)) {
+      const uint64_t dims[2] = {static_cast<uint64_t>(out_n), static_cast<uint64_t>(s.M)};
+      const uint64_t strides[1] = {static_cast<uint64_t>(a.ldo) * elem};
+      const uint32_t box[2] = {box_cols, kTileM};
+      ka.tma_out = encode_tiled(&mo, dt, 2, a.out, dims, strides, box, swz) == RB_OK;
+    }
   }
   const int key = s.BN * 4 + s.mt;
   switch (key) {
