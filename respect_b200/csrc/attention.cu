@@ -143,17 +143,21 @@ __device__ __forceinline__ bool node_allowed(const AttnDev& p, int row, int j) {
 // Node phase. A row's allowed node slots are visited in slot order, in
 // batches of up to 32. Lane u scores the batch's u-th slot (q.k over the 128
 // dims in ascending order, fp32, times scale*log2(e)), then the batch is folded
-// one slot at a time:
+// one slot at a time, starting from an empty state:
 //   m' = max(m, s); a = 2^(m - m'); p = 2^(s - m'); acc = p*v + acc*a; l = l*a + p
 // (lane u of the fold owns dims [4u, 4u+4)). Every slot goes through exactly
-// this arithmetic whatever the masking mode or batch boundaries, so a row's
-// bits depend only on its allowed slots and their order.
+// this arithmetic whatever the masking mode or batch boundaries, so the node
+// partial of a row depends only on its allowed slots and their order. The
+// output is then merge(prefix chunk 0, 1, ..., node partial), in that order.
 //
-// One block = one query row x one kv head; warp g serves query head
-// kvh*G + g (G = H / HK). The row's slots (committed, then trie ancestors, or
-// the allowed mask entries) are the same for all G heads, so each batch of
-// node K / V rows is staged in shared memory once for the whole group.
-constexpr int kMaxTrieDepth = 1024;
+// One item = one query row x one kv head; warp g serves query head kvh*G + g
+// (G = H / HK). The row's slots (committed, then trie ancestors, or the
+// allowed mask entries) are the same for all G heads, so each batch of node
+// K / V rows is staged in shared memory once for the whole group. A block
+// runs R items: their node folds before griddepcontrol.wait (they need only
+// q and the node K / V, which the kernel before the prefix kernel wrote, so
+// under PDL they run while the prefix kernel is still working), the merges
+// with the prefix chunk partials after it.
 constexpr int kChunkGroup = 4;  // chunk partials loaded together
 constexpr int kMaxGroup = 16;   // query heads per kv head handled by one block
 
@@ -161,6 +165,8 @@ template <typename T>
 struct NodeSmem {
   static constexpr int kRow = 128 * static_cast<int>(sizeof(T));  // bytes of one K / V row
   static constexpr int kKPitch = kRow + 16;                         // padded: conflict-free lane-per-row reads
+  static constexpr int kStage = 32 * (kKPitch + kRow);              // one batch of K and V rows
+  static int bytes(int G) { return kStage + G * 128 * 4; }          // + q of each head (fp32)
 };
 
 template <typename T>
@@ -199,110 +205,57 @@ __device__ __forceinline__ float dot128_smem<float>(const uint8_t* krow, const f
   return s;
 }
 
+// Running softmax state of one (row, head), lane-owned dims [4*lane, 4*lane+4).
+struct NodeAcc {
+  float m, l, acc[4];
+};
+
+// Fold `b` into `a` as the later piece: a = merge(a, b). Empty pieces (m = -inf) are skipped.
+__device__ __forceinline__ void merge_into(NodeAcc& a, float bm, float bl, const float (&bacc)[4]) {
+  if (bm == -INFINITY) return;
+  const float m_new = fmaxf(a.m, bm);
+  const float x = fast_exp2(a.m - m_new);
+  const float y = fast_exp2(bm - m_new);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) a.acc[e] = fmaf(bacc[e], y, a.acc[e] * x);
+  a.l = fmaf(bl, y, a.l * x);
+  a.m = m_new;
+}
+
+// The node fold of one item (block-uniform arguments; contains __syncthreads).
 template <typename T>
-__global__ void __launch_bounds__(32 * kMaxGroup) attn_nodes(const AttnDev p, const float* __restrict__ part) {
-  constexpr int D = 128;
+__device__ NodeAcc node_fold(const AttnDev& p, int row, int kvh, uint8_t* smem, int* slots, int* nslots) {
   using L = NodeSmem<T>;
-  __shared__ int chain[kMaxTrieDepth];
-  __shared__ int par_s[kMaxTrieDepth];
-  __shared__ int slots[32];
-  __shared__ int nslots;
-  __shared__ __align__(16) float qs[kMaxGroup][D];
-  // node K / V rows of the current batch (dynamic shared memory: 32 x (kKPitch + kRow) bytes)
-  extern __shared__ __align__(16) uint8_t node_smem[];
-  auto ks = reinterpret_cast<uint8_t(*)[L::kKPitch]>(node_smem);
-  auto vs = reinterpret_cast<uint8_t(*)[L::kRow]>(node_smem + 32 * L::kKPitch);
+  auto ks = reinterpret_cast<uint8_t(*)[L::kKPitch]>(smem);
+  auto vs = reinterpret_cast<uint8_t(*)[L::kRow]>(smem + 32 * L::kKPitch);
   const int G = p.H / p.HK;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x, kvh = blockIdx.y;
-  const int h = kvh * G + warp;
   const int nthr = G * 32;
-  pdl_trigger();
-  pdl_wait();
   const int d0 = lane * 4;
-  T* out = static_cast<T*>(p.out) + h * p.soh + static_cast<int64_t>(row) * p.som + d0;
-  const int live = p.sp ? p.sp->q : p.M;
-  if (row >= live) {  // padding row of a bucketed engine step: zeros, no reads
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (sizeof(T) == 2) reinterpret_cast<uint16_t*>(out)[e] = 0;
-      else reinterpret_cast<float*>(out)[e] = 0.f;
-    }
-    return;
-  }
+  float* qs = reinterpret_cast<float*>(smem + L::kStage) + warp * 128;
+  const int h = kvh * G + warp;
   const int NP = p.sp ? p.sp->prompt_len : p.NP;
-  const int nchunks = prefix_nchunks(NP, p.H);
   // Node slot 0 sits right after the prefix; without explicit node tensors
   // (engine path) the node segment is the same buffer from key NP on.
   const T* kn = p.kn ? static_cast<const T*>(p.kn) : static_cast<const T*>(p.kp) + static_cast<int64_t>(NP) * p.skpn;
   const T* vn = p.vn ? static_cast<const T*>(p.vn) : static_cast<const T*>(p.vp) + static_cast<int64_t>(NP) * p.svpn;
   const int64_t kbase = static_cast<int64_t>(kvh) * p.sknh, vbase = static_cast<int64_t>(kvh) * p.svnh;
-
-  // Trie mode: the row's ancestor chain (root first), walked once by thread 0.
+  const bool trie = p.mask_kind == kMaskTrie;
   int base = 0, depth = -1;
-  if (p.mask_kind == kMaskTrie) {
+  const int32_t* chain = nullptr;
+  if (trie) {
     base = p.sp ? p.sp->base : p.causal_first;
-    // parents of nodes 0..row, then the pointer chase runs in shared memory
-    for (int i = threadIdx.x; i <= row && i < kMaxTrieDepth; i += nthr) par_s[i] = p.parents[i];
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int dd = p.depths[row];
-      if (dd < 0 || dd >= kMaxTrieDepth || dd > row) {
-        raise_device_error(0x201);
-        dd = -1;
-      }
-      int a = row;
-      for (int t = dd; t >= 0; --t) {
-        chain[t] = a;
-        const int par = par_s[a];
-        if ((t > 0 && (par < 0 || par >= a)) || (t == 0 && par != -1)) {
-          raise_device_error(0x202);  // parents / depths inconsistent: fold nothing more
-          dd = -1;
-          break;
-        }
-        a = par;
-      }
-      nslots = dd;  // reuse as a broadcast of the depth
-    }
-    __syncthreads();
-    depth = nslots;
+    depth = p.depths[row];
+    if (depth < 0 || depth > row || depth >= p.chain_ld) depth = -1;  // invalid trie: reported when the chain was built
+    chain = p.chain + static_cast<int64_t>(row) * p.chain_ld;
   }
-
   float qv[4];
   ld4(static_cast<const T*>(p.q) + h * p.sqh + static_cast<int64_t>(row) * p.sqm + d0, qv);
-  *reinterpret_cast<float4*>(&qs[warp][d0]) = make_float4(qv[0], qv[1], qv[2], qv[3]);
+  *reinterpret_cast<float4*>(qs + d0) = make_float4(qv[0], qv[1], qv[2], qv[3]);
+  __syncwarp();
 
-  // Prefix chunk partials, merged in ascending chunk order.
-  float m = -INFINITY, l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int c0 = 0; c0 < nchunks; c0 += kChunkGroup) {
-    float cm[kChunkGroup], cl[kChunkGroup];
-    float4 ca[kChunkGroup];
-#pragma unroll
-    for (int g = 0; g < kChunkGroup; ++g) {
-      cm[g] = -INFINITY;
-      if (c0 + g < nchunks) {
-        const float* o = part + ((static_cast<int64_t>(c0 + g) * p.H + h) * p.M + row) * kPartStride;
-        cm[g] = o[D];
-        cl[g] = o[D + 1];
-        ca[g] = *reinterpret_cast<const float4*>(o + d0);
-      }
-    }
-#pragma unroll
-    for (int g = 0; g < kChunkGroup; ++g) {
-      if (cm[g] != -INFINITY) {
-        const float m_new = fmaxf(m, cm[g]);
-        const float a = fast_exp2(m - m_new);
-        const float b = fast_exp2(cm[g] - m_new);
-        acc[0] = fmaf(ca[g].x, b, acc[0] * a); acc[1] = fmaf(ca[g].y, b, acc[1] * a);
-        acc[2] = fmaf(ca[g].z, b, acc[2] * a); acc[3] = fmaf(ca[g].w, b, acc[3] * a);
-        l = fmaf(cl[g], b, l * a);
-        m = m_new;
-      }
-    }
-  }
-
+  NodeAcc r{-INFINITY, 0.f, {0.f, 0.f, 0.f, 0.f}};
   const float scale2 = p.sm_scale * kLog2e;
-  const bool trie = p.mask_kind == kMaskTrie;
   const int total = trie ? base + depth + 1 : p.NN;
   for (int b0 = 0; b0 < total; b0 += 32) {
     // 1. this batch's slots (in slot order)
@@ -320,10 +273,10 @@ __global__ void __launch_bounds__(32 * kMaxGroup) attn_nodes(const AttnDev p, co
       }
       const unsigned bits = __ballot_sync(0xffffffffu, v);
       if (v) slots[__popc(bits & ((1u << lane) - 1u))] = slot;
-      if (lane == 0) nslots = __popc(bits);
+      if (lane == 0) *nslots = __popc(bits);
     }
     __syncthreads();
-    const int cnt = nslots;
+    const int cnt = *nslots;
     if (cnt == 0) continue;
     // 2. stage the K / V rows of the batch (16-byte pieces, all threads)
     constexpr int kPieces = L::kRow / 16;
@@ -337,37 +290,120 @@ __global__ void __launch_bounds__(32 * kMaxGroup) attn_nodes(const AttnDev p, co
     }
     __syncthreads();
     // 3. scores (lane u <- slot u), then the ordered fold
-    const float sc = lane < cnt ? dot128_smem<T>(&ks[lane][0], qs[warp]) * scale2 : 0.f;
+    const float sc = lane < cnt ? dot128_smem<T>(&ks[lane][0], qs) * scale2 : 0.f;
     for (int u = 0; u < cnt; ++u) {
       const float su = __shfl_sync(0xffffffffu, sc, u);
       float vv[4];
       ld4(reinterpret_cast<const T*>(&vs[u][0]) + d0, vv);
-      const float m_new = fmaxf(m, su);
-      const float a = fast_exp2(m - m_new);
+      const float m_new = fmaxf(r.m, su);
+      const float a = fast_exp2(r.m - m_new);
       const float pe = fast_exp2(su - m_new);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[e] = fmaf(pe, vv[e], acc[e] * a);
-      l = fmaf(l, a, pe);
-      m = m_new;
+      for (int e = 0; e < 4; ++e) r.acc[e] = fmaf(pe, vv[e], r.acc[e] * a);
+      r.l = fmaf(r.l, a, pe);
+      r.m = m_new;
     }
   }
+  return r;
+}
+
+template <typename T, int R>
+__global__ void __launch_bounds__(32 * kMaxGroup) attn_nodes(const AttnDev p, const float* __restrict__ part) {
+  constexpr int D = 128;
+  __shared__ int slots[32];
+  __shared__ int nslots;
+  extern __shared__ __align__(16) uint8_t node_smem[];  // NodeSmem<T>::bytes(G)
+  const int G = p.H / p.HK;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int d0 = lane * 4;
+  const int live = p.sp ? p.sp->q : p.M;
+  const int n_items = p.M * p.HK;  // item i: row i % M, kv head i / M
+  pdl_trigger();
+
+  NodeAcc nd[R];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float v = __fdiv_rn(acc[e], l);
-    if (sizeof(T) == 2) reinterpret_cast<uint16_t*>(out)[e] = f32_to_bf16_bits(v);
-    else reinterpret_cast<float*>(out)[e] = v;
+  for (int it = 0; it < R; ++it) {
+    nd[it] = NodeAcc{-INFINITY, 0.f, {0.f, 0.f, 0.f, 0.f}};
+    const int item = blockIdx.x + it * gridDim.x;
+    if (item < n_items && item % p.M < live)  // uniform per block
+      nd[it] = node_fold<T>(p, item % p.M, item / p.M, node_smem, slots, &nslots);
+  }
+
+  pdl_wait();  // the prefix chunk partials are complete
+  const int NP = p.sp ? p.sp->prompt_len : p.NP;
+  const int nchunks = prefix_nchunks(NP, p.H);
+#pragma unroll
+  for (int it = 0; it < R; ++it) {
+    const int item = blockIdx.x + it * gridDim.x;
+    if (item >= n_items) continue;
+    const int row = item % p.M, h = (item / p.M) * G + warp;
+    T* out = static_cast<T*>(p.out) + h * p.soh + static_cast<int64_t>(row) * p.som + d0;
+    if (row >= live) {  // padding row of a bucketed engine step: zeros, no reads
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (sizeof(T) == 2) reinterpret_cast<uint16_t*>(out)[e] = 0;
+        else reinterpret_cast<float*>(out)[e] = 0.f;
+      }
+      continue;
+    }
+    // Prefix chunk partials in ascending chunk order, then the node partial.
+    NodeAcc r{-INFINITY, 0.f, {0.f, 0.f, 0.f, 0.f}};
+    for (int c0 = 0; c0 < nchunks; c0 += kChunkGroup) {
+      float cm[kChunkGroup], cl[kChunkGroup];
+      float ca[kChunkGroup][4];
+#pragma unroll
+      for (int g = 0; g < kChunkGroup; ++g) {
+        cm[g] = -INFINITY;
+        if (c0 + g < nchunks) {
+          const float* o = part + ((static_cast<int64_t>(c0 + g) * p.H + h) * p.M + row) * kPartStride;
+          cm[g] = o[D];
+          cl[g] = o[D + 1];
+          const float4 v = *reinterpret_cast<const float4*>(o + d0);
+          ca[g][0] = v.x; ca[g][1] = v.y; ca[g][2] = v.z; ca[g][3] = v.w;
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < kChunkGroup; ++g) merge_into(r, cm[g], cl[g], ca[g]);
+    }
+    merge_into(r, nd[it].m, nd[it].l, nd[it].acc);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float v = __fdiv_rn(r.acc[e], r.l);
+      if (sizeof(T) == 2) reinterpret_cast<uint16_t*>(out)[e] = f32_to_bf16_bits(v);
+      else reinterpret_cast<float*>(out)[e] = v;
+    }
   }
 }
 
+template <typename T, int R>
+static int launch_nodes_r(const AttnDev& p, const float* part, int grid, cudaStream_t stream, bool pdl) {
+  const int G = p.H / p.HK;
+  const int dyn = NodeSmem<T>::bytes(G);
+  if (cudaFuncSetAttribute(attn_nodes<T, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) != cudaSuccess)
+    return RB_ERR_CUDA;
+  return launch_k(attn_nodes<T, R>, dim3(grid), dim3(32 * G), dyn, stream, pdl, p, part);
+}
+
+// Items per block. One: a block's items run one after another (each a chain
+// of dependent loads, a block barrier per batch and a serial fold), so under
+// PDL more items per block made the pre-wait part outlast the prefix kernel
+// (measured on the config-3 step: 9.9 us after the prefix with one item,
+// 19.1 with two, 17.3 with three). The template keeps R for other shapes.
 template <typename T>
 static int launch_nodes(const AttnDev& p, const float* part, cudaStream_t stream, bool pdl) {
   const int G = p.H / p.HK;
   if (G > kMaxGroup) return RB_ERR_UNSUPPORTED;
-  using L = NodeSmem<T>;
-  constexpr int dyn = 32 * (L::kKPitch + L::kRow);
-  if (cudaFuncSetAttribute(attn_nodes<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) != cudaSuccess)
-    return RB_ERR_CUDA;
-  return launch_k(attn_nodes<T>, dim3(p.M, p.HK), dim3(32 * G), dyn, stream, pdl, p, part);
+  const int items = p.M * p.HK;
+  if (items <= 0) return RB_OK;
+  (void)pdl;
+  const int R = 1;
+  const int grid = (items + R - 1) / R;
+  switch (R) {
+    case 1: return launch_nodes_r<T, 1>(p, part, grid, stream, pdl);
+    case 2: return launch_nodes_r<T, 2>(p, part, grid, stream, pdl);
+    case 3: return launch_nodes_r<T, 3>(p, part, grid, stream, pdl);
+    default: return launch_nodes_r<T, 4>(p, part, grid, stream, pdl);
+  }
 }
 
 // ----------------------------------------------------------------- host
@@ -445,7 +481,7 @@ int attn_launch(const rb_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t s
   return launch_nodes<uint16_t>(p, part, stream, false);
 }
 
-// Engine path: bf16, q/base/PL from device memory, trie masking from parents.
+// Engine path: bf16, q/base/PL from device memory, trie masking from the ancestor chains.
 int attn_launch_engine(const AttnDev& p, float* part, int max_chunks, const CUtensorMap& tq,
                        const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t stream) {
   const int st = attn_prefix_tc_launch(tq, tk, tv, p, part, max_chunks, stream, true);

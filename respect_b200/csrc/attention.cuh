@@ -47,13 +47,14 @@ struct StepParams {
 };
 
 // Node masking modes beyond the public rb_mask_kind values.
-constexpr int kMaskTrie = 16;  // committed slots [0, base) then the row's ancestors, from parents[]
+constexpr int kMaskTrie = 16;  // committed slots [0, base) then the row's ancestors, from chain[]
 
 struct AttnDev {
   int H, M, HK, NP, NN;
   const StepParams* sp;       // non-null: q, base and NP come from device memory
-  const int32_t* parents;     // kMaskTrie
-  const int32_t* depths;      // kMaskTrie
+  const int32_t* depths;      // kMaskTrie: depth of every node
+  const int32_t* chain;       // kMaskTrie: row r's ancestors root first, chain[r * chain_ld + t], t <= depth
+  int chain_ld;
   const void* q; int64_t sqh, sqm;
   const void* kp; int64_t skph, skpn;
   const void* vp; int64_t svph, svpn;

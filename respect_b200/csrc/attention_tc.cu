@@ -59,11 +59,16 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   const int C = prefix_chunk(NP, p.H);
   const int k0 = c * C;
   const int k1 = min(NP, k0 + C);
-  if (k0 >= k1 || rt * kRows >= M) return;  // uniform per CTA, before any barrier exists
+  // Dependents (the node kernel) are released only after this grid's wait: they
+  // read q and the node K / V before their own wait, so every CTA, including
+  // one without work, releases them only once the kernel before this one is done.
+  if (k0 >= k1 || rt * kRows >= M) {  // uniform per CTA, before any barrier exists
+    pdl_wait();
+    return;
+  }
   const int ntiles = (k1 - k0 + kKeys - 1) / kKeys;
   const int kvh = h / (p.H / p.HK);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  pdl_trigger();
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tq);
@@ -89,6 +94,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_wait();  // q / K / V come from the previous kernels
+  pdl_trigger();
   const uint32_t sQ = smem_u32(smem + kQOff), sKV = smem_u32(smem + kKVOff), sP = smem_u32(smem + kPOff);
 
   if (warp == kProducerWarp) {

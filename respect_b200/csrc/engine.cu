@@ -49,18 +49,45 @@ __device__ __forceinline__ float row_inv_rms(const float* v, int cnt, int N, flo
 }
 
 constexpr int kMaxPerThread = 32;  // hidden <= 32 * NT (NT = 1024 for hidden >= 2048)
+constexpr int kMaxChainRows = 1024;  // max_rows limit of an engine
+
 
 // h[row] = embed[ids[row]];  xn[row] = rmsnorm(h[row], w). EPT: elements per thread.
+// Also the row's ancestor chain for the attention node phase of every layer:
+// chain[row * ld + t] = the ancestor at depth t (t = 0 root .. depth[row] = row),
+// walked once per step from the parent array (parents precede children).
 template <int NT, int EPT>
 __global__ void __launch_bounds__(NT) embed_norm_kernel(const StepParams* __restrict__ sp, const int32_t* __restrict__ ids,
                                                         const uint16_t* __restrict__ emb, const uint16_t* __restrict__ w,
                                                         uint16_t* __restrict__ h, uint16_t* __restrict__ xn, int N,
-                                                        int vocab, float eps) {
+                                                        int vocab, float eps, const int32_t* __restrict__ parents,
+                                                        const int32_t* __restrict__ depths, int32_t* __restrict__ chain,
+                                                        int chain_ld) {
   __shared__ float red[NT / 32];
+  __shared__ int par_s[kMaxChainRows];
   const int row = blockIdx.x;
   pdl_trigger();
   pdl_wait();
   if (row >= sp->q) return;
+  for (int i = threadIdx.x; i <= row && i < kMaxChainRows; i += NT) par_s[i] = parents[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int dd = depths[row];
+    if (dd < 0 || dd > row || dd >= chain_ld || row >= kMaxChainRows) {
+      raise_device_error(0x201);
+      dd = -1;
+    }
+    int a = row;
+    for (int t = dd; t >= 0; --t) {
+      chain[static_cast<int64_t>(row) * chain_ld + t] = a;
+      const int par = par_s[a];
+      if ((t > 0 && (par < 0 || par >= a)) || (t == 0 && par != -1)) {
+        raise_device_error(0x202);  // parents / depths inconsistent
+        break;
+      }
+      a = par;
+    }
+  }
   int id = ids[row];
   if (id < 0 || id >= vocab) {
     raise_device_error(0x301);
@@ -260,7 +287,7 @@ struct rb_engine {
   int nsm = 148;
   // workspace carve-up
   StepParams* d_params = nullptr;
-  int32_t *d_ids = nullptr, *d_parents = nullptr, *d_depths = nullptr;
+  int32_t *d_ids = nullptr, *d_parents = nullptr, *d_depths = nullptr, *d_chain = nullptr;
   int64_t* d_out = nullptr;
   uint16_t *h = nullptr, *xn = nullptr, *qbuf = nullptr, *attn = nullptr, *act = nullptr;
   float *part = nullptr, *apart = nullptr, *logits = nullptr;
@@ -287,7 +314,7 @@ constexpr int kQkvNT = 128;
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
-  size_t params, ids, parents, depths, out, keys, h, xn, qbuf, attn, act, part, apart, logits, total;
+  size_t params, ids, parents, depths, chain, out, keys, h, xn, qbuf, attn, act, part, apart, logits, total;
 };
 
 Layout layout_of(const rb_model_config& c) {
@@ -310,6 +337,7 @@ Layout layout_of(const rb_model_config& c) {
   L.ids = take(R * 4);
   L.parents = take(R * 4);
   L.depths = take(R * 4);
+  L.chain = take(R * R * 4);
   L.out = take(R * 8);
   L.keys = take(R * 8);
   L.h = take(R * c.hidden * 2);
@@ -399,7 +427,8 @@ int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
     return launch_k(embed_norm_kernel<NT, EPT>, dim3(rows), dim3(NT), 0, st, true,
                     static_cast<const StepParams*>(e->d_params), static_cast<const int32_t*>(e->d_ids),
                     static_cast<const uint16_t*>(e->w.embed), static_cast<const uint16_t*>(e->layers[0].in_norm),
-                    e->h, e->xn, hid, c.vocab, c.rms_eps);
+                    e->h, e->xn, hid, c.vocab, c.rms_eps, static_cast<const int32_t*>(e->d_parents),
+                    static_cast<const int32_t*>(e->d_depths), e->d_chain, c.max_rows);
   }));
   for (int l = 0; l < c.n_layers; ++l) {
     const rb_layer_weights& lw = e->layers[l];
@@ -420,8 +449,9 @@ int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
     AttnDev p{};
     p.H = H; p.M = rows; p.HK = HK; p.NP = 0; p.NN = 0;
     p.sp = e->d_params;
-    p.parents = e->d_parents;
     p.depths = e->d_depths;
+    p.chain = e->d_chain;
+    p.chain_ld = c.max_rows;
     p.q = e->qbuf; p.sqh = static_cast<int64_t>(rows) * D; p.sqm = D;
     const int64_t sh = static_cast<int64_t>(c.max_slots) * D;
     p.kp = e->kc[l]; p.skph = sh; p.skpn = D;
@@ -514,6 +544,7 @@ int rb_engine_create(const rb_model_config* cfg, const rb_model_weights* w, void
   e->d_ids = reinterpret_cast<int32_t*>(base + L.ids);
   e->d_parents = reinterpret_cast<int32_t*>(base + L.parents);
   e->d_depths = reinterpret_cast<int32_t*>(base + L.depths);
+  e->d_chain = reinterpret_cast<int32_t*>(base + L.chain);
   e->d_out = reinterpret_cast<int64_t*>(base + L.out);
   e->keys = reinterpret_cast<unsigned long long*>(base + L.keys);
   e->h = reinterpret_cast<uint16_t*>(base + L.h);
