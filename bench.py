@@ -90,6 +90,23 @@ def config_block(n):
             "parallelism": f"replicas{n}", "l2": "inputs larger than L2 (14.1 GB weights per step)"}
 
 
+# ------------------------------------------------------------------ multi-rank helpers
+def reduce_max(x: float, device) -> float:
+    """The maximum of x over all ranks (x itself without a process group)."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return float(x)
+    t = torch.tensor([float(x)], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_value(world: int, units_per_step: float, steps: int, ms: float) -> float:
+    """Whole-job throughput: every rank processed units_per_step per step; ms is the max over ranks."""
+    return world * units_per_step * steps / (ms / 1e3)
+
+
 # ------------------------------------------------------------------ CPU sample (oracle)
 def cpu_sample(steps, warmup, seed=0):
     """One decoder layer of the step (128 rows vs the 3000-token prefix) plus 1/28
@@ -111,14 +128,19 @@ def cpu_sample(steps, warmup, seed=0):
     tree = build_trie(top_up(rng, chain_seqs(rng, 4, CHAIN, V // 28), NODES, V // 28))
     kc = [round_bf16(rng.standard_normal((HK, PROMPT + NODES, D), dtype=np.float32))]
     vc = [round_bf16(rng.standard_normal((HK, PROMPT + NODES, D), dtype=np.float32))]
+    # all host threads (torchrun sets OMP_NUM_THREADS=1 for its workers; the
+    # BLAS pool is raised explicitly and the count actually in use reported)
+    from threadpoolctl import threadpool_info, threadpool_limits
     times = []
-    for i in range(warmup + steps):
-        t0 = time.perf_counter()
-        omodel.verify_step(W, cfg, tree.tokens(), tree.parents(), tree.depths(), PROMPT, 0, kc, vc)
-        if i >= warmup:
-            times.append(time.perf_counter() - t0)
+    with threadpool_limits(limits=os.cpu_count() or 1):
+        pools = [p["num_threads"] for p in threadpool_info()]
+        for i in range(warmup + steps):
+            t0 = time.perf_counter()
+            omodel.verify_step(W, cfg, tree.tokens(), tree.parents(), tree.depths(), PROMPT, 0, kc, vc)
+            if i >= warmup:
+                times.append(time.perf_counter() - t0)
     t_step = 28 * statistics.median(times)
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    threads = max(pools) if pools else 1
     return dict(value=CHAIN / t_step, unit="committed tokens/s", cores=threads, kind="port",
                 sample=("numpy oracle (oracle/model.py), one full-size decoder layer of the config-3 step "
                         "(128 trie rows vs a 3000-token prefix) plus 1/28 of the lm_head rows; "
@@ -256,18 +278,13 @@ def run_native(args):
             fn()
         e1.record(st)
         torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
+        return reduce_max(e0.elapsed_time(e1), dev)
 
     with Clocks(local) as clk:
         ms = timed(device_step, args.steps)
     clocks = clk.summary()
     ms_step = ms / args.steps
-    value = world * committed * args.steps / (ms / 1e3)
+    value = job_value(world, committed, args.steps, ms)
 
     # e2e: the public verify call with host trie arrays, host read-back, host walk, compaction
     def e2e_step():
@@ -279,7 +296,7 @@ def run_native(args):
     for _ in range(2):
         e2e_step()
     ms2 = timed(e2e_step, k2)
-    e2e = {"value": world * committed * k2 / (ms2 / 1e3), "unit": "committed tokens/s",
+    e2e = {"value": job_value(world, committed, k2, ms2), "unit": "committed tokens/s",
            "ms_per_step": ms2 / k2, "h2d_bytes_per_step": 32 + 3 * 4 * NODES, "d2h_bytes_per_step": 8 * NODES}
 
     # roofline of the dominant kernel: the fused gate|up + SiLU*mul GEMM of a layer
