@@ -117,10 +117,14 @@ __global__ void __launch_bounds__(NT) embed_norm_kernel(const StepParams* __rest
 }
 
 // o = bf16(sum_s partial[s]);  h = bf16(h + o);  xn = rmsnorm(h, w)
-// Splits are summed in ascending order (as splitk_reduce does); the split loop
-// is outermost so every split's loads of a thread are in flight together.
+// Splits are summed in ascending order (as splitk_reduce does). Beyond 8
+// splits the split loads of two columns are in flight together, not all of
+// them: with the 40-register cap that keeps the block from spilling, and the
+// cap lets the CTA of the next (weight-streaming) GEMM fit on the SM beside it
+// and start its weight stream while this kernel runs (with every load in
+// flight the block took the whole register file).
 template <int NT, int EPT, int MAXS>
-__global__ void __launch_bounds__(NT) resid_norm_kernel(const StepParams* __restrict__ sp, const float* __restrict__ part,
+__global__ void __maxnreg__(40) resid_norm_kernel(const StepParams* __restrict__ sp, const float* __restrict__ part,
                                                         int splits, int M, uint16_t* __restrict__ h,
                                                         const uint16_t* __restrict__ w, uint16_t* __restrict__ xn, int N,
                                                         float eps) {
@@ -144,6 +148,7 @@ __global__ void __launch_bounds__(NT) resid_norm_kernel(const StepParams* __rest
     for (int s = 1; s < MAXS; ++s)
       if (s < splits) a += t[s];
     acc[k] = a;
+    if (MAXS > 8 && (k & 1)) asm volatile("" ::: "memory");  // no later column's loads hoisted above this point
   }
   float v[EPT];
 #pragma unroll
@@ -404,6 +409,7 @@ int launch_resid_norm(rb_engine* e, int splits, int rows, const void* w, cudaStr
     };
     if (splits <= 4) return go(std::integral_constant<int, 4>{});
     if (splits <= 8) return go(std::integral_constant<int, 8>{});
+    if (splits <= 12) return go(std::integral_constant<int, 12>{});
     if (splits <= 16) return go(std::integral_constant<int, 16>{});
     return static_cast<int>(RB_ERR_UNSUPPORTED);
   });

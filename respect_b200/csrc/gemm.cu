@@ -407,6 +407,13 @@ GemmShape gemm_plan(int M, int N, int K, int num_sms, int force_bn, int force_sp
     bn = force_bn;
   } else {
     const int n256 = (N + 255) / 256;
+    // Few weight tiles over a short K: 128-wide tiles with half the K splits.
+    // A split GEMM writes splits x M x N fp32 partials that the next kernel
+    // sums, and fewer splits halve that traffic; it pays while each CTA's
+    // activation re-reads (K / splits columns per tile) stay short. Measured on
+    // the config-3 step: faster for q|k|v (N 4608, K 3584) and o (3584 x 3584),
+    // slower for down (K 18944), which keeps 256.
+    if (n256 * 4 <= num_sms && s.k_chunks <= 128) bn = 128;
     if (n256 > num_sms) {
       // Many weight tiles: pick the width whose last wave is the fullest.
       const int cands[3] = {256, 208, 128};
