@@ -34,6 +34,7 @@ constexpr int kBarOff = kPOff + 2 * kHalf;   // 192 KB
 constexpr int kRedOff = kBarOff + 256;       // row max / row sum exchange: 2 x 2 x 128 floats
 constexpr int kSmem = 1024 + kRedOff + 512 * 4;
 static_assert(kSmem <= 232448, "shared memory budget");
+static_assert(kRows * kPartStride * 4 <= 2 * kStage, "partial block staged in the K/V buffers");
 constexpr int kSoftmaxThreads = 256;
 constexpr int kThreads = kSoftmaxThreads + 64;
 constexpr int kProducerWarp = 8, kMmaWarp = 9;
@@ -182,35 +183,41 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       }
       // Row max on the raw scores (scale2 > 0 and rounding are monotone, so
       // max(s)*scale2 == max(s*scale2)); keys past the chunk end are masked.
-      float mx = -INFINITY;
-      const bool full = nvalid >= 64;
-      if (full) {
+      if (nvalid < 64) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(raw[i >> 4][i & 15]));
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
+        for (int i = 0; i < 64; ++i)
           if (i >= nvalid) raw[i >> 4][i & 15] = __float_as_uint(-INFINITY);
-          mx = fmaxf(mx, __uint_as_float(raw[i >> 4][i & 15]));
-        }
       }
+      // pairwise tree (max is exact, so any grouping gives the same value)
+      float t32[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        t32[i] = fmaxf(__uint_as_float(raw[i >> 4][i & 15]), __uint_as_float(raw[(i + 32) >> 4][(i + 32) & 15]));
+#pragma unroll
+      for (int w2 = 16; w2 >= 1; w2 >>= 1)
+#pragma unroll
+        for (int i = 0; i < w2; ++i) t32[i] = fmaxf(t32[i], t32[i + w2]);
+      float mx = t32[0];
       red[hf * 128 + r] = mx * scale2;
       named_bar(1, kSoftmaxThreads);
       mx = fmaxf(red[r], red[128 + r]);
       const float m_new = fmaxf(m, mx);  // finite: every tile has a valid key in its lower half
       const float alpha = fast_exp2(m - m_new);
       const float neg_m = -m_new;
-      float rs = 0.f;
       uint32_t w[32];
 #pragma unroll
       for (int i = 0; i < 64; i += 2) {
         // p = 2^(s*scale2 - m'); a masked key (-inf) gives exactly 0
         const float p0 = fast_exp2(fmaf(__uint_as_float(raw[i >> 4][i & 15]), scale2, neg_m));
         const float p1 = fast_exp2(fmaf(__uint_as_float(raw[(i + 1) >> 4][(i + 1) & 15]), scale2, neg_m));
-        rs += p0;
-        rs += p1;
+        t32[i / 2] = p0 + p1;  // the row sum: a fixed pairwise tree over the 64 keys
         w[i / 2] = pack_bf16x2(p0, p1);
       }
+#pragma unroll
+      for (int w2 = 16; w2 >= 1; w2 >>= 1)
+#pragma unroll
+        for (int i = 0; i < w2; ++i) t32[i] += t32[i + w2];
+      const float rs = t32[0];
       red[256 + hf * 128 + r] = rs;
       if (j > 0 && ok) {
         // P_{j-1} V_{j-1} must be complete before P_j overwrites P and O is rescaled.
@@ -257,16 +264,25 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
 #pragma unroll
       for (int i = 0; i < 64; ++i) acc[i] = __uint_as_float(raw[i >> 4][i & 15]);
     }
+    // The 128 rows' partials are one contiguous block of the partial buffer
+    // ([row][kPartStride] floats): stage it in the K/V buffers (free once the
+    // last P V is done) and write it with one bulk copy.
     const int row = rt * kRows + r;
+    float* st = reinterpret_cast<float*>(smem + kKVOff) + r * kPartStride;
     if (ok && row < M) {
-      float* o = part + ((static_cast<int64_t>(c) * p.H + h) * p.M + row) * kPartStride;
 #pragma unroll
       for (int i = 0; i < 64; i += 4)
-        *reinterpret_cast<float4*>(o + hf * 64 + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
-      if (hf == 0) {
-        o[kD] = m;
-        o[kD + 1] = l;
-      }
+        *reinterpret_cast<float4*>(st + hf * 64 + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+      if (hf == 0) *reinterpret_cast<float4*>(st + kD) = make_float4(m, l, 0.f, 0.f);
+    }
+    fence_proxy_async_smem();
+    named_bar(1, kSoftmaxThreads);
+    if (threadIdx.x == 0) {
+      const int rows = min(kRows, M - rt * kRows);
+      bulk_store(part + ((static_cast<int64_t>(c) * p.H + h) * p.M + rt * kRows) * kPartStride, sKV,
+                 static_cast<uint32_t>(rows * kPartStride * 4));
+      bulk_commit();
+      bulk_wait_read();  // the staging block has been read before the CTA may exit
     }
   }
   tc_fence_before();

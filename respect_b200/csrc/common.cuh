@@ -145,6 +145,13 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, uint32_t src,
                "r"(src), "r"(x), "r"(y), "r"(z)
                : "memory");
 }
+// Plain (untiled) bulk copy shared::cta -> global; both addresses 16-byte
+// aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+               "r"(src), "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Every committed bulk store has finished reading its shared-memory source (the
 // buffer may be reused and the CTA may exit; the global writes are performed by
