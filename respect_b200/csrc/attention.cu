@@ -158,7 +158,7 @@ __device__ __forceinline__ bool node_allowed(const AttnDev& p, int row, int j) {
 // q and the node K / V, which the kernel before the prefix kernel wrote, so
 // under PDL they run while the prefix kernel is still working), the merges
 // with the prefix chunk partials after it.
-constexpr int kChunkGroup = 4;  // chunk partials loaded together
+constexpr int kChunkGroup = 2;  // chunk partials loaded together
 constexpr int kMaxGroup = 16;   // query heads per kv head handled by one block
 
 template <typename T>
@@ -174,7 +174,7 @@ __device__ __forceinline__ float dot128_smem(const uint8_t* krow, const float* q
 template <>
 __device__ __forceinline__ float dot128_smem<uint16_t>(const uint8_t* krow, const float* qs) {
   float s = 0.f;
-#pragma unroll
+#pragma unroll 4
   for (int c = 0; c < 16; ++c) {
     const uint4 k8 = reinterpret_cast<const uint4*>(krow)[c];
     const float4 qa = reinterpret_cast<const float4*>(qs)[2 * c];
@@ -307,8 +307,12 @@ __device__ NodeAcc node_fold(const AttnDev& p, int row, int kvh, uint8_t* smem, 
   return r;
 }
 
+// 48 registers a thread: a block of 7 warps then fits in the register-file
+// partitions a prefix CTA (10 warps at ~136 registers) leaves free, so under
+// PDL one node block per SM folds while the prefix kernel runs (at 64
+// registers none could: two of its warps exceed what is left in a partition).
 template <typename T, int R>
-__global__ void __launch_bounds__(32 * kMaxGroup) attn_nodes(const AttnDev p, const float* __restrict__ part) {
+__global__ void __maxnreg__(48) attn_nodes(const AttnDev p, const float* __restrict__ part) {
   constexpr int D = 128;
   __shared__ int slots[32];
   __shared__ int nslots;
@@ -387,8 +391,8 @@ static int launch_nodes_r(const AttnDev& p, const float* part, int grid, cudaStr
 // Items per block. One: a block's items run one after another (each a chain
 // of dependent loads, a block barrier per batch and a serial fold), so under
 // PDL more items per block made the pre-wait part outlast the prefix kernel
-// (measured on the config-3 step: 9.9 us after the prefix with one item,
-// 19.1 with two, 17.3 with three). The template keeps R for other shapes.
+// (measured on the config-3 step: 9.7 us after the prefix with one item,
+// 17.8 with two, 17.3 with three). The template keeps R for other shapes.
 template <typename T>
 static int launch_nodes(const AttnDev& p, const float* part, cudaStream_t stream, bool pdl) {
   const int G = p.H / p.HK;
