@@ -36,7 +36,7 @@ def trie_with_path(rng, path_tokens, n_nodes, vocab, n_chains=4):
     while the merged trie stays within n_nodes), topped up to n_nodes."""
     L = len(path_tokens)
     seqs = [tuple(path_tokens)]
-    for _ in range(n_chains - 1):
+    for _ in range(n_chains - 1 if L > 1 else 0):
         share = int(rng.integers(1, L))
         cand = tuple(path_tokens[:share]) + tuple(int(t) for t in rng.integers(0, vocab, L - share))
         if len(build_trie(seqs + [cand]).nodes) <= n_nodes:
@@ -207,31 +207,53 @@ def test_7b_trie_vs_ar_bitwise(big):
         assert torch.equal(ka, kb) and torch.equal(va, vb)
 
 
-@pytest.mark.parametrize("P", [2999, 3071, 3072, 3073, 3129])
-def test_7b_invariance_sweep(big, P):
-    """Config 4: the same 32-token path inside tries of 32/64/256/512 nodes gives
-    bitwise identical committed-node logits, at prefix lengths around tile
-    boundaries."""
+# Config 4 prefix lengths: 2,999 .. 3,129 every 8 (every 128-key tile boundary of the
+# prefix chunks lies between two of them) plus both sides of 3,072.
+SWEEP_P = sorted(set(range(2999, 3130, 8)) | {3071, 3072, 3073, 3129}, reverse=True)
+
+
+def _path_rows(tree, path_toks):
+    idx, node = [], tree.roots[path_toks[0]]
+    for d in range(len(path_toks)):
+        idx.append(node)
+        if d + 1 < len(path_toks):
+            node = tree.nodes[node].children[path_toks[d + 1]]
+    return idx
+
+
+def test_7b_invariance_sweep(big):
+    """Config 4: a fixed 32-token path, inside tries of 1 / 8 / 64 / 256 / 512 nodes
+    (the path's first n tokens where n < 32; seeded siblings top up the rest), at
+    every prefix length of SWEEP_P: the committed-node logits and K / V equal the
+    same tokens decoded one at a time (1-node steps), bitwise.
+
+    One prefill of 3,129 tokens serves every prefix length: a token's KV depends
+    only on the tokens before it, and the lengths run from the longest down, so a
+    step's node writes (slots >= P) never touch a later case's prefix."""
     cfg, w, eng = big
-    rng = np.random.default_rng(P)
-    eng.prefill(rng.integers(0, cfg.vocab, P))
+    rng = np.random.default_rng(44)
+    eng.prefill(rng.integers(0, cfg.vocab, max(SWEEP_P)))
     path_toks = [int(t) for t in rng.integers(0, cfg.vocab, 32)]
-    ref = None
-    for n in (32, 64, 256, 512):
-        tree = trie_with_path(np.random.default_rng(n), path_toks, n, cfg.vocab)
-        assert len(tree.nodes) == n
-        eng.step(tree.tokens().astype(np.int32), tree.parents(), tree.depths(), 0, P)
-        # node index of the path's d-th token: follow the trie from the root
-        idx, node = [], tree.roots[path_toks[0]]
-        for d in range(32):
-            idx.append(node)
-            if d + 1 < 32:
-                node = tree.nodes[node].children[path_toks[d + 1]]
-        rows = eng.logits(n)[idx].clone()
-        kv = [(k[:, P + torch.tensor(idx, device=DEV)].clone()) for k in eng.kc[:2]]
-        if ref is None:
-            ref = (rows, kv)
-        else:
-            assert torch.equal(rows, ref[0])
-            for a, b in zip(kv, ref[1]):
-                assert torch.equal(a, b)
+    for P in SWEEP_P:
+        # token-by-token reference: path token i as a 1-node step after i committed tokens
+        ar_rows, ar_k = [], []
+        for i, t in enumerate(path_toks):
+            eng.step(np.array([t], np.int32), np.array([-1], np.int32), np.array([0], np.int32), i, P)
+            ar_rows.append(eng.logits(1)[0].clone())
+        ar_k = [k[:, P:P + 32].clone() for k in eng.kc[:2]]
+        ar_v = [v[:, P:P + 32].clone() for v in eng.vc[:2]]
+        for n in (1, 8, 64, 256, 512):
+            L = min(n, 32)
+            tree = trie_with_path(np.random.default_rng(n + P), path_toks[:L], n, cfg.vocab)
+            # the path inserted last: its nodes past the shared prefixes take the last slots
+            tree = build_trie(list(tree.seqs[1:]) + [tree.seqs[0]])
+            assert len(tree.nodes) == n
+            eng.step(tree.tokens().astype(np.int32), tree.parents(), tree.depths(), 0, P)
+            idx = _path_rows(tree, path_toks[:L])
+            lg = eng.logits(n)
+            for d, node in enumerate(idx):
+                assert torch.equal(lg[node], ar_rows[d]), (P, n, d)
+            sl = P + torch.tensor(idx, device=DEV)
+            for li in range(2):
+                assert torch.equal(eng.kc[li][:, sl], ar_k[li][:, :L]), (P, n, li)
+                assert torch.equal(eng.vc[li][:, sl], ar_v[li][:, :L]), (P, n, li)
