@@ -38,13 +38,19 @@ static_assert(kRows * kPartStride * 4 <= 2 * kStage, "partial block staged in th
 constexpr int kSoftmaxThreads = 256;
 constexpr int kThreads = kSoftmaxThreads + 64;
 constexpr int kProducerWarp = 8, kMmaWarp = 9;
-// barrier indices
-enum { Q_FULL = 0, KV_FULL = 1, KV_EMPTY = 3, S_FULL = 5, P_FULL = 7, O_FULL = 8, NBAR = 9 };
+// barrier indices. K and V of a stage have their own full / empty barriers: K is
+// free again once Q K^T is done (early in a tile), V once P V is (at its end),
+// so the next tile but one's K is requested a whole softmax earlier than a
+// shared K/V barrier would allow, which keeps the TMA latency off the critical path.
+enum { Q_FULL = 0, K_FULL = 1, V_FULL = 3, K_EMPTY = 5, V_EMPTY = 7, S_FULL = 9, P_FULL = 11, O_FULL = 12, NBAR = 13 };
+constexpr float kRescaleSlack = 8.0f;
 constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, 0, 0);
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, 0, 1);
 }  // namespace tc
 
-__global__ void __launch_bounds__(tc::kThreads, 1)
+// At most 136 registers: the CTA's 10 warps then leave a register-file partition
+// room for two warps of the node kernel (48 registers), which folds beside it.
+__global__ void __maxnreg__(136)
     attn_prefix_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, const AttnDev p, float* __restrict__ part) {
   using namespace tc;
@@ -76,10 +82,12 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     tma_prefetch_desc(&tk);
     tma_prefetch_desc(&tv);
     mbar_init(bar(Q_FULL), 1);
-    mbar_init(bar(KV_FULL), 1);
-    mbar_init(bar(KV_FULL + 1), 1);
-    mbar_init(bar(KV_EMPTY), 1);
-    mbar_init(bar(KV_EMPTY + 1), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(K_FULL + i), 1);
+      mbar_init(bar(V_FULL + i), 1);
+      mbar_init(bar(K_EMPTY + i), 1);
+      mbar_init(bar(V_EMPTY + i), 1);
+    }
     mbar_init(bar(S_FULL), 1);
     mbar_init(bar(S_FULL + 1), 1);
     mbar_init(bar(P_FULL), kSoftmaxThreads);
@@ -104,16 +112,20 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       mbar_arrive_expect_tx(bar(Q_FULL), 2 * kHalf);
       tma_load_3d(sQ, &tq, bar(Q_FULL), 0, rt * kRows, h, pol);
       tma_load_3d(sQ + kHalf, &tq, bar(Q_FULL), 64, rt * kRows, h, pol);
+      // K(j) and V(j) in the order their stages free up (K(j) after Q K^T of
+      // tile j-2, V(j) after P V of tile j-2).
       for (int j = 0; j < ntiles; ++j) {
         const int s = j & 1;
-        if (j >= 2 && !mbar_wait(bar(KV_EMPTY + s), ((j >> 1) & 1) ^ 1, 0x211)) break;
         const uint32_t st = sKV + s * kStage;
         const int key = k0 + j * kKeys;
-        mbar_arrive_expect_tx(bar(KV_FULL + s), kStage);
-        tma_load_3d(st, &tk, bar(KV_FULL + s), 0, key, kvh, pol);
-        tma_load_3d(st + kHalf, &tk, bar(KV_FULL + s), 64, key, kvh, pol);
-        tma_load_3d(st + 2 * kHalf, &tv, bar(KV_FULL + s), 0, key, kvh, pol);
-        tma_load_3d(st + 3 * kHalf, &tv, bar(KV_FULL + s), 64, key, kvh, pol);
+        if (j >= 2 && !mbar_wait(bar(K_EMPTY + s), ((j >> 1) & 1) ^ 1, 0x211)) break;
+        mbar_arrive_expect_tx(bar(K_FULL + s), 2 * kHalf);
+        tma_load_3d(st, &tk, bar(K_FULL + s), 0, key, kvh, pol);
+        tma_load_3d(st + kHalf, &tk, bar(K_FULL + s), 64, key, kvh, pol);
+        if (j >= 2 && !mbar_wait(bar(V_EMPTY + s), ((j >> 1) & 1) ^ 1, 0x21a)) break;
+        mbar_arrive_expect_tx(bar(V_FULL + s), 2 * kHalf);
+        tma_load_3d(st + 2 * kHalf, &tv, bar(V_FULL + s), 0, key, kvh, pol);
+        tma_load_3d(st + 3 * kHalf, &tv, bar(V_FULL + s), 64, key, kvh, pol);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -127,20 +139,22 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           umma_bf16(d, sdesc_kmajor_sw128(sQ + off), sdesc_kmajor_sw128(st + off), kIdescQK, kk ? 1u : 0u);
         }
         umma_commit(bar(S_FULL + (j & 1)));
+        if (j + 2 < ntiles) umma_commit(bar(K_EMPTY + (j & 1)));  // K(j) read: the stage takes K(j+2)
       };
-      bool ok = mbar_wait(bar(Q_FULL), 0, 0x212) && mbar_wait(bar(KV_FULL), 0, 0x213);
+      bool ok = mbar_wait(bar(Q_FULL), 0, 0x212) && mbar_wait(bar(K_FULL), 0, 0x213);
       if (ok) {
         tc_fence_after();
         issue_qk(0);
       }
       for (int j = 0; ok && j < ntiles; ++j) {
         if (j + 1 < ntiles) {
-          if (!mbar_wait(bar(KV_FULL + ((j + 1) & 1)), ((j + 1) >> 1) & 1, 0x214)) break;
+          if (!mbar_wait(bar(K_FULL + ((j + 1) & 1)), ((j + 1) >> 1) & 1, 0x214)) break;
           tc_fence_after();
           issue_qk(j + 1);
         }
-        // P_j written and O rescaled by alpha_j (both signalled by P_FULL)
-        if (!mbar_wait(bar(P_FULL), j & 1, 0x215)) break;
+        // P_j written and O rescaled by alpha_j (both signalled by P_FULL), V_j loaded
+        if (!mbar_wait(bar(P_FULL), j & 1, 0x215) || !mbar_wait(bar(V_FULL + (j & 1)), (j >> 1) & 1, 0x21b))
+          break;
         tc_fence_after();
         const uint32_t sv = sKV + (j & 1) * kStage + 2 * kHalf;
 #pragma unroll
@@ -150,7 +164,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
                     (j | kk) ? 1u : 0u);
         }
         umma_commit(bar(O_FULL));
-        if (j + 2 < ntiles) umma_commit(bar(KV_EMPTY + (j & 1)));
+        if (j + 2 < ntiles) umma_commit(bar(V_EMPTY + (j & 1)));  // V(j) read: the stage takes V(j+2)
       }
     }
   } else {
@@ -201,7 +215,13 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       red[hf * 128 + r] = mx * scale2;
       named_bar(1, kSoftmaxThreads);
       mx = fmaxf(red[r], red[128 + r]);
-      const float m_new = fmaxf(m, mx);  // finite: every tile has a valid key in its lower half
+      // Lazy rescaling: the running max moves (and O, l are rescaled) only when
+      // the tile's max exceeds it by more than kRescaleSlack (log2 units);
+      // otherwise the stale max stays and p = 2^(s - m) may reach 2^kRescaleSlack,
+      // well inside bf16 and fp32 range. O / l is unchanged mathematically, the
+      // O round trip through TMEM is skipped in most tiles, and the decision
+      // depends on the row's own scores only.
+      const float m_new = (mx > m + kRescaleSlack) ? mx : m;  // finite after the first tile (valid keys)
       const float alpha = fast_exp2(m - m_new);
       const float neg_m = -m_new;
       uint32_t w[32];
