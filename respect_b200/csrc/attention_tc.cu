@@ -31,8 +31,8 @@ constexpr int kKVOff = 2 * kHalf;            // 2 stages x (K 2 halves, V 2 halv
 constexpr int kStage = 4 * kHalf;            // 64 KB
 constexpr int kPOff = kKVOff + 2 * kStage;   // P: 2 halves (keys 0-63 | 64-127)
 constexpr int kBarOff = kPOff + 2 * kHalf;   // 192 KB
-constexpr int kRedOff = kBarOff + 256;       // row max / row sum exchange: 2 x 2 x 128 floats
-constexpr int kSmem = 1024 + kRedOff + 512 * 4;
+constexpr int kRedOff = kBarOff + 256;       // row max / row sum exchange: [2 tiles][2][2 halves][128] floats
+constexpr int kSmem = 1024 + kRedOff + 1024 * 4;
 static_assert(kSmem <= 232448, "shared memory budget");
 static_assert(kRows * kPartStride * 4 <= 2 * kStage, "partial block staged in the K/V buffers");
 constexpr int kSoftmaxThreads = 256;
@@ -173,9 +173,12 @@ __global__ void __maxnreg__(136)
     const int q4 = warp & 3, hf = warp >> 2;
     const int r = q4 * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
-    float* red = reinterpret_cast<float*>(smem + kRedOff);  // [2 (max|sum)][2 (half)][128] floats
+    // Row max / row sum exchange, double-buffered by tile parity: tile j's
+    // sums are read after tile j+1's max barrier (every thread has written
+    // them by then), so a tile needs one block barrier, not two.
+    float* red_all = reinterpret_cast<float*>(smem + kRedOff);  // [2 (tile)][2 (max|sum)][2 (half)][128] floats
     const float scale2 = p.sm_scale * 1.4426950408889634f;
-    float m = -INFINITY, l = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
     // A timed-out wait (device error already raised) skips this warp's TMEM
     // work but never a named barrier, so the other warps cannot block.
     bool ok = true;
@@ -212,9 +215,14 @@ __global__ void __maxnreg__(136)
 #pragma unroll
         for (int i = 0; i < w2; ++i) t32[i] = fmaxf(t32[i], t32[i + w2]);
       float mx = t32[0];
+      float* red = red_all + (j & 1) * 512;
       red[hf * 128 + r] = mx * scale2;
       named_bar(1, kSoftmaxThreads);
       mx = fmaxf(red[r], red[128 + r]);
+      if (j > 0) {  // the previous tile's row sum, now written by both halves
+        const float* prev = red_all + ((j - 1) & 1) * 512 + 256;
+        l = fmaf(l, alpha_prev, prev[r] + prev[128 + r]);
+      }
       // Lazy rescaling: the running max moves (and O, l are rescaled) only when
       // the tile's max exceeds it by more than kRescaleSlack (log2 units);
       // otherwise the stale max stays and p = 2^(s - m) may reach 2^kRescaleSlack,
@@ -268,9 +276,13 @@ __global__ void __maxnreg__(136)
       fence_proxy_async_smem();  // P stores -> visible to the tensor core (async proxy)
       tc_fence_before();         // S loads and O stores of this tile ordered before the arrive
       mbar_arrive(bar(P_FULL));
-      named_bar(1, kSoftmaxThreads);
-      l = fmaf(l, alpha, red[256 + r] + red[384 + r]);
+      alpha_prev = alpha;
       m = m_new;
+    }
+    named_bar(1, kSoftmaxThreads);  // the last tile's row sums
+    if (ntiles > 0) {
+      const float* prev = red_all + ((ntiles - 1) & 1) * 512 + 256;
+      l = fmaf(l, alpha_prev, prev[r] + prev[128 + r]);
     }
     // the last P V product, then O leaves TMEM once
     float acc[64];
