@@ -131,6 +131,12 @@ __global__ void __maxnreg__(40) resid_norm_kernel(const StepParams* __restrict__
   __shared__ float red[NT / 32];
   const int row = blockIdx.x;
   pdl_trigger();
+  uint16_t wv[EPT];  // the norm weights never change: read before waiting for the GEMM
+#pragma unroll
+  for (int k = 0; k < EPT; ++k) {
+    const int i = threadIdx.x + k * NT;
+    wv[k] = i < N ? w[i] : 0;
+  }
   pdl_wait();
   if (row >= sp->q) return;
   const int64_t plane = static_cast<int64_t>(M) * N;
@@ -168,7 +174,7 @@ __global__ void __maxnreg__(40) resid_norm_kernel(const StepParams* __restrict__
     const int i = threadIdx.x + k * NT;
     if (i < N) {
       const float xh = round_bf16(v[k] * r);
-      xn[static_cast<int64_t>(row) * N + i] = f32_to_bf16_bits(bf16_bits_to_f32(w[i]) * xh);
+      xn[static_cast<int64_t>(row) * N + i] = f32_to_bf16_bits(bf16_bits_to_f32(wv[k]) * xh);
     }
   }
 }
@@ -188,8 +194,32 @@ __global__ void __launch_bounds__(128) qkv_finish_kernel(
   const int head = blockIdx.y * 4 + warp;
   const int nh = H + 2 * HK;
   pdl_trigger();
-  pdl_wait();
   if (row >= sp->q || head >= nh) return;
+  // Before the wait: the norm weights and the rotary rows (StepParams and the
+  // depths are copied in before the step's first kernel).
+  const int slot = sp->prompt_len + sp->base + row;
+  const bool vhead = head >= H + HK;
+  float wq[4] = {0.f, 0.f, 0.f, 0.f}, cr[4] = {0.f, 0.f, 0.f, 0.f}, sr[4] = {0.f, 0.f, 0.f, 0.f};
+  if (!vhead) {
+    const uint16_t* w = head < H ? qn_w : kn_w;
+    int pos = sp->prompt_len + sp->base + depths[row] + sp->rope_delta;
+    if (pos < 0 || pos >= max_pos) {
+      raise_device_error(0x303);
+      pos = 0;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int d = lane + 32 * k;
+      wq[k] = bf16_bits_to_f32(w[d]);
+      cr[k] = bf16_bits_to_f32(cos_t[static_cast<int64_t>(pos) * D + d]);
+      sr[k] = bf16_bits_to_f32(sin_t[static_cast<int64_t>(pos) * D + d]);
+    }
+  }
+  pdl_wait();
+  if (slot >= max_slots) {
+    raise_device_error(0x302);
+    return;
+  }
   const int N = nh * D;
   const int64_t plane = static_cast<int64_t>(M) * N;
   float x[4];
@@ -202,18 +232,12 @@ __global__ void __launch_bounds__(128) qkv_finish_kernel(
   }
 #pragma unroll
   for (int k = 0; k < 4; ++k) x[k] = round_bf16(x[k]);
-  const int slot = sp->prompt_len + sp->base + row;
-  if (slot >= max_slots) {
-    raise_device_error(0x302);
-    return;
-  }
-  if (head >= H + HK) {  // v head
+  if (vhead) {  // v head
     uint16_t* dst = vc + (head - H - HK) * kv_s_head + static_cast<int64_t>(slot) * D;
 #pragma unroll
     for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = f32_to_bf16_bits(x[k]);
     return;
   }
-  const uint16_t* w = head < H ? qn_w : kn_w;
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < 4; ++k) ss = fmaf(x[k], x[k], ss);
@@ -222,21 +246,13 @@ __global__ void __launch_bounds__(128) qkv_finish_kernel(
   const float r = rsqrtf((0.f + ss) / static_cast<float>(D) + eps);
   float y[4];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) y[k] = round_bf16(bf16_bits_to_f32(w[lane + 32 * k]) * round_bf16(x[k] * r));
-  int pos = sp->prompt_len + sp->base + depths[row] + sp->rope_delta;
-  if (pos < 0 || pos >= max_pos) {
-    raise_device_error(0x303);
-    pos = 0;
-  }
-  const uint16_t* cr = cos_t + static_cast<int64_t>(pos) * D;
-  const uint16_t* sr = sin_t + static_cast<int64_t>(pos) * D;
+  for (int k = 0; k < 4; ++k) y[k] = round_bf16(wq[k] * round_bf16(x[k] * r));
   float o[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const int d = lane + 32 * k;
     const float xr = k < 2 ? -y[k + 2] : y[k - 2];  // rotate_half: d < 64 takes -x[d+64]
-    const float a = round_bf16(__fmul_rn(y[k], bf16_bits_to_f32(cr[d])));
-    const float b = round_bf16(__fmul_rn(xr, bf16_bits_to_f32(sr[d])));
+    const float a = round_bf16(__fmul_rn(y[k], cr[k]));
+    const float b = round_bf16(__fmul_rn(xr, sr[k]));
     o[k] = round_bf16(__fadd_rn(a, b));
   }
   uint16_t* dst;
