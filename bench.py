@@ -286,18 +286,22 @@ def run_native(args):
     ms_step = ms / args.steps
     value = job_value(world, committed, args.steps, ms)
 
-    # e2e: the public verify call with host trie arrays, host read-back, host walk, compaction
+    # e2e: the public calls with host trie arrays (copied in), the acceptance walk and
+    # KV compaction on the device, and the acceptance record read back to the host
+    h_ids, h_par, h_dep = tree.tokens().astype(np.int32), tree.parents(), tree.depths()
+
     def e2e_step():
-        am = eng.verify(tree, PROMPT, 0)
-        p, a, r = walk(tree, first, 1 << 30, -1, lambda x, ch: int(am[ch]))
-        eng.compact(p, PROMPT, 0)
+        eng.step(h_ids, h_par, h_dep, 0, PROMPT)
+        p, a, r = eng.accept(first, 1 << 30, -1, n=NODES)
+        assert len(a) == committed
 
     k2 = args.e2e_steps or max(1, args.steps // 3)
     for _ in range(2):
         e2e_step()
     ms2 = timed(e2e_step, k2)
     e2e = {"value": job_value(world, committed, k2, ms2), "unit": "committed tokens/s",
-           "ms_per_step": ms2 / k2, "h2d_bytes_per_step": 32 + 3 * 4 * NODES, "d2h_bytes_per_step": 8 * NODES}
+           "ms_per_step": ms2 / k2, "h2d_bytes_per_step": 32 + 3 * 4 * NODES, "d2h_bytes_per_step": 4 * (4 + 2 * NODES),
+           "path": "VerifyEngine.step (host trie arrays) + VerifyEngine.accept (device walk + KV compaction)"}
 
     # roofline of the dominant kernel: the fused gate|up + SiLU*mul GEMM of a layer
     hbm, tf, src = measured_peaks()

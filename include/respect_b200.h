@@ -21,6 +21,7 @@
  *   rb_verify_mask      respect/decoding/verify.py:35-41     additive 4-D trie mask
  *   rb_engine_*         respect/decoding/verify.py:12-46 + respect/kernels/patch.py:70-107
  *                       (one verify forward of the whole decoder with the dedicated kernels)
+ *   rb_engine_accept    respect/decoding/acceptance.py:26-46 + kv_buffer.py:93-104 on the device
  */
 #ifndef RESPECT_B200_H
 #define RESPECT_B200_H
@@ -287,6 +288,16 @@ RB_API int rb_engine_fetch_ids(rb_engine* e, int64_t* host, int n, void* stream)
 /* kv_buffer.py:93-104 for every layer: slots prompt_len + base + path[i] move
  * to prompt_len + base + i (path = accepted node indices, host array). */
 RB_API int rb_engine_compact(rb_engine* e, const int32_t* path, int n, int prompt_len, int base, void* stream);
+/* The acceptance walk (acceptance.py:26-46) and the compaction (kv_buffer.py:93-104)
+ * of the last step on the device, without a host round trip: from the step's
+ * trie and greedy picks, the accepted chain (root holding `first`, each next
+ * node holding the pick after its parent, stopping after `eos` or `cap` tokens)
+ * is recorded and its KV moved to slots prompt_len + base + i. Enqueue on the
+ * step's stream after rb_engine_step. rb_engine_fetch_accept copies the record
+ * to host as [count, correction, base, prompt_len, path[0..n), tokens[0..n)]
+ * (count <= n needs n >= the trie size or >= cap). */
+RB_API int rb_engine_accept(rb_engine* e, int first, int cap, int eos, void* stream);
+RB_API int rb_engine_fetch_accept(rb_engine* e, int32_t* host, int n, void* stream);
 
 #ifdef __cplusplus
 }

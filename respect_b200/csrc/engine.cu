@@ -18,6 +18,7 @@
 // so an engine step is bitwise equal to composing rb_linear / rb_rmsnorm /
 // rb_rope / rb_silu_mul / rb_fused_attn_hyb, and a row's results never depend
 // on how many rows the step carries.
+#include <climits>
 #include <map>
 #include <vector>
 
@@ -299,6 +300,101 @@ __global__ void argmax_keys_kernel(const StepParams* __restrict__ sp, const floa
 // ------------------------------------------------------------------ host engine
 using namespace rb;
 
+// ------------------------------------------------------------ acceptance on the device
+// The acceptance walk of respect/decoding/acceptance.py:26-46 over the step's
+// trie and greedy picks, without the host: node j is accepted iff its root
+// holds `first`, every node below the root holds the pick after its parent,
+// no strict ancestor holds `eos`, and depth(j) < cap (parents precede
+// children, a node has at most one child per token, so the accepted nodes form
+// one chain, one per depth). Record: [count, correction, base, prompt_len,
+// path[max_rows], tokens[max_rows]]; the correction is the pick after the last
+// accepted node (eos when that node is eos; `first` when nothing is accepted).
+constexpr int kAcceptHdr = 4;
+__global__ void __launch_bounds__(1024) accept_kernel(const StepParams* __restrict__ sp, const int32_t* __restrict__ ids,
+                                                      const int32_t* __restrict__ parents,
+                                                      const int32_t* __restrict__ depths,
+                                                      const int64_t* __restrict__ picks, int first, int cap, int eos,
+                                                      int max_rows, int32_t* __restrict__ rec) {
+  __shared__ int32_t s_ids[kMaxChainRows], s_par[kMaxChainRows], s_pick[kMaxChainRows], s_path[kMaxChainRows];
+  const int q = min(sp->q, kMaxChainRows);
+  for (int j = threadIdx.x; j < q; j += blockDim.x) {
+    s_ids[j] = ids[j];
+    s_par[j] = parents[j];
+    s_pick[j] = static_cast<int32_t>(picks[j]);
+    s_path[j] = INT_MAX;
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < q; j += blockDim.x) {
+    const int d = depths[j];
+    if (d < 0 || d >= cap || d >= q) continue;
+    bool ok = true;
+    int c = j, steps = 0;
+    while (ok) {
+      const int par = s_par[c];
+      if (par < 0) {
+        ok = s_ids[c] == first && steps == d;
+        break;
+      }
+      if (par >= c || steps >= d) {  // malformed trie (the host validates it): accept nothing here
+        ok = false;
+        break;
+      }
+      ok = s_ids[c] == s_pick[par] && s_ids[par] != eos;
+      c = par;
+      ++steps;
+    }
+    if (ok) atomicMin(&s_path[d], j);  // one node per depth in a valid trie; lowest index otherwise
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int lim = min(cap, q);
+    int n = 0;
+    while (n < lim && s_path[n] != INT_MAX) ++n;
+    int corr = first;
+    if (n > 0) {
+      const int last = s_path[n - 1];
+      corr = s_ids[last] == eos ? eos : s_pick[last];
+    }
+    rec[0] = n;
+    rec[1] = corr;
+    rec[2] = sp->base;
+    rec[3] = sp->prompt_len;
+  }
+  __syncthreads();
+  const int n = rec[0];
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    rec[kAcceptHdr + i] = s_path[i];
+    rec[kAcceptHdr + max_rows + i] = s_ids[s_path[i]];
+  }
+}
+
+// kv_buffer.py:93-104 driven by the acceptance record: slot PL + base + path[i]
+// moves to PL + base + i for every layer, head, K and V (each thread moves one
+// 16-byte piece of every accepted slot, in ascending order, so the moves that
+// overlap read their source before it is overwritten).
+struct KvLayers {
+  void* k[RB_COMPACT_MAX_LAYERS];
+  void* v[RB_COMPACT_MAX_LAYERS];
+};
+__global__ void compact_record_kernel(const __grid_constant__ KvLayers kv, int n_layers, int HK, int64_t s_head,
+                                      int64_t s_slot, const int32_t* __restrict__ rec, int max_slots) {
+  constexpr int kPieces = 128 * 2 / 16;  // 16-byte pieces of one bf16 row of 128
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (tid >= static_cast<int64_t>(n_layers) * 2 * HK * kPieces) return;
+  const int n = rec[0], start = rec[3] + rec[2];
+  const int piece = static_cast<int>(tid % kPieces);
+  const int h = static_cast<int>((tid / kPieces) % HK);
+  const int which = static_cast<int>((tid / (kPieces * HK)) % 2);
+  const int layer = static_cast<int>(tid / (static_cast<int64_t>(kPieces) * HK * 2));
+  uint8_t* base = static_cast<uint8_t*>(which ? kv.v[layer] : kv.k[layer]) + h * s_head * 2 + piece * 16;
+  for (int i = 0; i < n; ++i) {
+    const int src = start + rec[kAcceptHdr + i], dst = start + i;
+    if (src == dst || src >= max_slots) continue;
+    const uint4 val = *reinterpret_cast<const uint4*>(base + static_cast<int64_t>(src) * s_slot * 2);
+    *reinterpret_cast<uint4*>(base + static_cast<int64_t>(dst) * s_slot * 2) = val;
+  }
+}
+
 struct rb_engine {
   rb_model_config cfg;
   rb_model_weights w;
@@ -308,7 +404,7 @@ struct rb_engine {
   int nsm = 148;
   // workspace carve-up
   StepParams* d_params = nullptr;
-  int32_t *d_ids = nullptr, *d_parents = nullptr, *d_depths = nullptr, *d_chain = nullptr;
+  int32_t *d_ids = nullptr, *d_parents = nullptr, *d_depths = nullptr, *d_chain = nullptr, *d_accept = nullptr;
   int64_t* d_out = nullptr;
   uint16_t *h = nullptr, *xn = nullptr, *qbuf = nullptr, *attn = nullptr, *act = nullptr;
   float *part = nullptr, *apart = nullptr, *logits = nullptr;
@@ -335,7 +431,7 @@ constexpr int kQkvNT = 128;
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
-  size_t params, ids, parents, depths, chain, out, keys, h, xn, qbuf, attn, act, part, apart, logits, total;
+  size_t params, ids, parents, depths, chain, accept, out, keys, h, xn, qbuf, attn, act, part, apart, logits, total;
 };
 
 Layout layout_of(const rb_model_config& c) {
@@ -359,6 +455,7 @@ Layout layout_of(const rb_model_config& c) {
   L.parents = take(R * 4);
   L.depths = take(R * 4);
   L.chain = take(R * R * 4);
+  L.accept = take((kAcceptHdr + 2 * R) * 4);
   L.out = take(R * 8);
   L.keys = take(R * 8);
   L.h = take(R * c.hidden * 2);
@@ -567,6 +664,7 @@ int rb_engine_create(const rb_model_config* cfg, const rb_model_weights* w, void
   e->d_parents = reinterpret_cast<int32_t*>(base + L.parents);
   e->d_depths = reinterpret_cast<int32_t*>(base + L.depths);
   e->d_chain = reinterpret_cast<int32_t*>(base + L.chain);
+  e->d_accept = reinterpret_cast<int32_t*>(base + L.accept);
   e->d_out = reinterpret_cast<int64_t*>(base + L.out);
   e->keys = reinterpret_cast<unsigned long long*>(base + L.keys);
   e->h = reinterpret_cast<uint16_t*>(base + L.h);
@@ -753,6 +851,38 @@ int rb_engine_compact(rb_engine* e, const int32_t* path, int n, int prompt_len, 
   return compact_launch(e->kc.data(), e->vc.data(), c.n_layers, c.n_kv_heads, c.head_dim,
                         static_cast<int64_t>(c.max_slots) * c.head_dim, c.head_dim, 2, src.data(), n,
                         prompt_len + base, static_cast<cudaStream_t>(stream));
+}
+
+int rb_engine_accept(rb_engine* e, int first, int cap, int eos, void* stream) {
+  if (!e || cap < 0) return RB_ERR_INVALID_ARG;
+  const rb_model_config& c = e->cfg;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  accept_kernel<<<1, 1024, 0, st>>>(e->d_params, e->d_ids, e->d_parents, e->d_depths, e->d_out, first, cap, eos,
+                                    c.max_rows, e->d_accept);
+  if (cudaGetLastError() != cudaSuccess) return RB_ERR_CUDA;
+  KvLayers kv{};
+  for (int l = 0; l < c.n_layers; ++l) {
+    kv.k[l] = e->kc[l];
+    kv.v[l] = e->vc[l];
+  }
+  const int64_t total = static_cast<int64_t>(c.n_layers) * 2 * c.n_kv_heads * (128 * 2 / 16);
+  compact_record_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(
+      kv, c.n_layers, c.n_kv_heads, static_cast<int64_t>(c.max_slots) * c.head_dim, c.head_dim, e->d_accept,
+      c.max_slots);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;
+}
+
+int rb_engine_fetch_accept(rb_engine* e, int32_t* host, int n, void* stream) {
+  if (!e || !host || n < 0 || n > e->cfg.max_rows) return RB_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t hdr = kAcceptHdr * 4, nb = static_cast<size_t>(n) * 4;
+  if (cudaMemcpyAsync(host, e->d_accept, hdr, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      (n > 0 && (cudaMemcpyAsync(host + kAcceptHdr, e->d_accept + kAcceptHdr, nb, cudaMemcpyDeviceToHost, st) !=
+                     cudaSuccess ||
+                 cudaMemcpyAsync(host + kAcceptHdr + n, e->d_accept + kAcceptHdr + e->cfg.max_rows, nb,
+                                 cudaMemcpyDeviceToHost, st) != cudaSuccess)))
+    return RB_ERR_CUDA;
+  return RB_OK;
 }
 
 }  // extern "C"

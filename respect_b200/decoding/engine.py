@@ -91,6 +91,8 @@ _ENGINE_SIGS = {
     "rb_engine_fetch_ids": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "rb_engine_compact": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), ctypes.c_int,
                                          ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "rb_engine_accept": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "rb_engine_fetch_accept": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
 }
 _lib.SIGNATURES.update(_ENGINE_SIGS)
 
@@ -252,6 +254,21 @@ class VerifyEngine:
         _lib.call("rb_engine_compact", self._h, arr, len(path), prompt_len, base, st.cuda_stream)
 
     # ------------------------------------------------------------------ helpers
+    def accept(self, first: int, cap: int, eos: int, n: int | None = None, stream=None):
+        """The acceptance walk and the KV compaction of the last step, on the device
+        (rb_engine_accept): returns (path, tokens, correction) like
+        respect_b200.decoding.acceptance.walk, with the accepted KV already moved to
+        prompt_len + base + i. n bounds the record read back (default: max_rows)."""
+        st = stream or torch.cuda.current_stream(self.device)
+        n = self.max_rows if n is None else n
+        _lib.call("rb_engine_accept", self._h, int(first), int(cap), int(eos), st.cuda_stream)
+        rec = torch.empty(4 + 2 * n, dtype=torch.int32, pin_memory=True)
+        _lib.call("rb_engine_fetch_accept", self._h, rec.data_ptr(), n, st.cuda_stream)
+        st.synchronize()
+        r = rec.tolist()
+        cnt = r[0]
+        return r[4:4 + cnt], r[4 + n:4 + n + cnt], r[1]
+
     def verify(self, tree: Trie, prompt_len: int, base: int, act_off: int = 0, act_size: int = 0,
                graph: bool = True) -> np.ndarray:
         """verify_trie + greedy_token for a host trie: returns the greedy ids per node (host)."""

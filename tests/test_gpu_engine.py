@@ -175,6 +175,39 @@ def test_engine_equals_operator_composition_7b_layer():
         eng.close()
 
 
+def test_device_accept_matches_host_walk(tiny):
+    """rb_engine_accept (walk + compaction on the device) equals the host walk
+    (acceptance.py:26-46) followed by rb_engine_compact: the same path, tokens and
+    correction token, and the same KV bits, for full acceptance, a cap, an EOS
+    inside the accepted chain and a first token that no root holds."""
+    from respect_b200.decoding.acceptance import walk
+    cfg, w, eng = tiny
+    rng = np.random.default_rng(9)
+    P = 64
+    eng.prefill(rng.integers(0, cfg.vocab, P))
+    first = int(rng.integers(0, cfg.vocab))
+    toks, _ = ar_decode(eng, first, 12, P)
+    tree = trie_with_path(rng, toks[:12], 48, cfg.vocab)
+    tree = build_trie(list(tree.seqs[1:]) + [tree.seqs[0]])  # the chain's deep nodes on the last slots
+    q = len(tree.nodes)
+    absent = next(t for t in range(cfg.vocab) if t not in tree.roots)
+    cases = [(toks[0], 100, -1), (toks[0], 5, -1), (toks[0], 100, toks[6]), (absent, 100, -1)]
+    args = (tree.tokens().astype(np.int32), tree.parents(), tree.depths(), 0, P)
+    for first_tok, cap, eos in cases:
+        eng.step(*args)
+        ids = eng.fetch_ids(q)
+        path_h, acc_h, rec_h = walk(tree, first_tok, cap, eos, lambda a, ch: int(ids[ch]))
+        eng.compact(path_h, P, 0)
+        kv_host = kv_slots(eng, P, P + q)
+        eng.step(*args)
+        path_d, acc_d, rec_d = eng.accept(first_tok, cap, eos)
+        assert (path_d, acc_d, rec_d) == (path_h, acc_h, rec_h), (first_tok, cap, eos)
+        for (ka, va), (kb, vb) in zip(kv_host, kv_slots(eng, P, P + q)):
+            assert torch.equal(ka, kb) and torch.equal(va, vb)
+    # the chain was accepted in full in the first case, cut by the cap and by the EOS in the next two
+    assert len(walk(tree, toks[0], 100, -1, lambda a, ch: int(ids[ch]))[0]) >= 10
+
+
 @pytest.fixture(scope="module")
 def big():
     cfg = DecoderConfig.baseline_7b()
