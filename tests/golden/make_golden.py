@@ -13,6 +13,10 @@ What runs (all on CPU, in the build container where the reference is importable)
     causal mask, padding-row trick)                                    -> kernels.npz
   * PyTorch eager RoPE (q*cos + rotate_half(q)*sin) and silu(g)*u in
     bf16: the outputs respect/system/fused.py reproduces bitwise      -> kernels.npz
+  * respect.candidates.datastore.Datastore lookups (static / drive /
+    added / drive-only indexes, key lengths 1-3) and
+    respect.candidates.history.CocHistory / first_token_filter on seeded
+    sentences                                                          -> candidates.json
   * a 2-layer random-init Qwen3-VL text model verified through
     respect.decoding.verify.verify_trie with and without
     respect.kernels.patch.dedicated_kernels, fp32                       -> model.npz
@@ -213,10 +217,51 @@ def gen_kernels(out):
     np.savez_compressed(out / "kernels.npz", **arrays)
 
 
+def candidate_inputs(seed=17):
+    """Seeded sentences over a small vocabulary (so keys repeat), lookup prefixes and history frames."""
+    rng = np.random.default_rng(seed)
+    sent = lambda lo, hi: tuple(int(t) for t in rng.integers(0, 8, int(rng.integers(lo, hi))))
+    static = [sent(1, 12) for _ in range(40)]
+    drive = [sent(2, 10) for _ in range(12)]
+    added = [sent(2, 9) for _ in range(6)]
+    prefixes = [[int(t) for t in rng.integers(0, 9, int(rng.integers(0, 5)))] for _ in range(60)]
+    frames = [sent(0, 6) for _ in range(14)]
+    return dict(static=static, drive=drive, added=added, prefixes=prefixes, frames=frames)
+
+
+def gen_candidates(out):
+    from respect.candidates.datastore import Datastore
+    from respect.candidates.history import CocHistory, first_token_filter
+    inp = candidate_inputs()
+    eos = 8
+    res = {"inputs": {k: [list(x) for x in v] for k, v in inp.items()}, "eos": eos, "lookups": [], "history": []}
+    def record(gmax, name, d):
+        for cmax in (1, 3, 64):
+            res["lookups"].append(dict(gmax=gmax, stage=name, cmax=cmax,
+                                       out=[[list(c) for c in d.lookup(pfx, cmax)] for pfx in inp["prefixes"]]))
+
+    for gmax in (1, 2, 3):
+        ds = Datastore(inp["static"], gmax=gmax).with_drive(inp["drive"])
+        record(gmax, "static+drive", ds)            # before the drive index grows
+        for s in inp["added"]:
+            ds.add(s)
+        record(gmax, "after_add", ds)
+        record(gmax, "drive_only", ds.without_static())
+        record(gmax, "static_only", Datastore(inp["static"], gmax=gmax))
+        res.setdefault("num_entries", []).append(Datastore(inp["static"], gmax=gmax).num_entries())
+    h = CocHistory(eos)
+    for f, s in enumerate(inp["frames"]):
+        h.append(f, list(s) + [eos] * (f % 3))
+        res["history"].append([[list(c) for c in h.candidates(n)] for n in range(0, 7)])
+    cands = [tuple(s) for s in inp["static"][:20]]
+    res["first_token"] = [[list(c) for c in first_token_filter(cands, t)] for t in range(10)]
+    (out / "candidates.json").write_text(json.dumps(res))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("RESPECT_REF"), required=os.environ.get("RESPECT_REF") is None)
-    ap.add_argument("--only", default="trie,verify,kernels,model")
+    ap.add_argument("--only", default="trie,verify,kernels,model,candidates")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.ref).resolve()))
     only = set(args.only.split(","))
@@ -227,6 +272,8 @@ def main():
         gen_verify_mask(HERE)
     if "kernels" in only:
         gen_kernels(HERE)
+    if "candidates" in only:
+        gen_candidates(HERE)
     if "model" in only:
         sys.path.insert(0, str(HERE))
         import make_model_golden
