@@ -14,6 +14,7 @@
  *   rb_rmsnorm          respect/kernels/rmsnorm.py:25-32     rmsnorm
  *   rb_rope             respect/system/fused.py:67-75        rope
  *   rb_silu_mul         respect/system/fused.py:116-123      silu_mul
+ *   rb_add_sq, rb_norm_apply  respect/system/fused.py:126-194 add_sq / norm_from (Prefill)
  *   rb_linear_swiglu_packed  fused.py:106-123 silu_mul fused into the gate|up linear (patch.py:26-37)
  *   rb_greedy_token     respect/decoding/acceptance.py:11-23 mask_action_vocab + greedy_token
  *   rb_compact_kv       respect/decoding/kv_buffer.py:93-104 compact
@@ -169,6 +170,18 @@ RB_API int rb_rope(const void* x, int64_t sxb, int64_t sxh, int64_t sxl, int64_t
  * dtype RB_F32: y = (g / (1 + exp(-g))) * u in fp32 (the reference's eager
  * branch for non-bf16 inputs, fused.py:117-118). Contiguous, n elements. */
 RB_API int rb_silu_mul(const void* g, const void* u, void* y, int64_t n, int dtype, void* stream);
+
+/* ------------------------------------------------------------------ prefill norm pieces
+ * respect/system/fused.py:126-194 (add_sq, norm_from): the elementwise parts of
+ * an eager residual add + RMSNorm, bit for bit, around the row mean of squares
+ * that the caller computes with PyTorch. rb_add_sq: x = r + h in the promoted
+ * dtype (bf16 only when both are bf16), sq = x * x in fp32; h = NULL gives
+ * sq = r * r alone (x unused). rb_norm_apply: y = w * to_x_dtype(x * rsqrt(var
+ * + eps)), var [M] fp32, y in promote(w, x). Contiguous [M, N] / [n] tensors. */
+RB_API int rb_add_sq(const void* r, const void* h, void* x, float* sq, int64_t n, int r_dtype, int h_dtype,
+                     int x_dtype, void* stream);
+RB_API int rb_norm_apply(const void* x, const float* var, const void* w, void* y, int64_t M, int N, float eps,
+                         int x_dtype, int w_dtype, int y_dtype, void* stream);
 
 /* ------------------------------------------------------------------ greedy token
  * out[m] = argmax_v logits[m, v] with v in [offset, offset + size) excluded;

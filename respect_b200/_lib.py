@@ -73,6 +73,9 @@ SIGNATURES = {
     "rb_rope": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                         c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),
     "rb_silu_mul": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p]),
+    "rb_add_sq": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p]),
+    "rb_norm_apply": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_int, c_int, c_int,
+                              c_void_p]),
     "rb_greedy_token": (c_int, [c_void_p, c_int, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "rb_compact_kv": (c_int, [ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p), c_int, c_int, c_int,
                               c_int64, c_int64, c_int, ctypes.POINTER(ctypes.c_int32), c_int, c_int,

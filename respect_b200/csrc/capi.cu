@@ -161,6 +161,22 @@ int rb_rope(const void* x, int64_t sxb, int64_t sxh, int64_t sxl, int64_t sxd, c
                      as_stream(stream));
 }
 
+int rb_add_sq(const void* r, const void* h, void* x, float* sq, int64_t n, int r_dtype, int h_dtype, int x_dtype,
+              void* stream) {
+  if (n < 0 || !r || !sq || (h && !x)) return RB_ERR_INVALID_ARG;
+  for (int t : {r_dtype, h ? h_dtype : RB_F32, h ? x_dtype : RB_F32})
+    if (t != RB_F32 && t != RB_BF16) return RB_ERR_UNSUPPORTED;
+  return add_sq_launch(r, h, x, sq, n, r_dtype, h_dtype, x_dtype, as_stream(stream));
+}
+
+int rb_norm_apply(const void* x, const float* var, const void* w, void* y, int64_t M, int N, float eps, int x_dtype,
+                  int w_dtype, int y_dtype, void* stream) {
+  if (M < 0 || N <= 0 || !x || !var || !w || !y) return RB_ERR_INVALID_ARG;
+  for (int t : {x_dtype, w_dtype, y_dtype})
+    if (t != RB_F32 && t != RB_BF16) return RB_ERR_UNSUPPORTED;
+  return norm_apply_launch(x, var, w, y, M, N, eps, x_dtype, w_dtype, y_dtype, as_stream(stream));
+}
+
 int rb_silu_mul(const void* g, const void* u, void* y, int64_t n, int dtype, void* stream) {
   if (n < 0 || (n > 0 && (!g || !u || !y))) return RB_ERR_INVALID_ARG;
   return silu_mul_launch(g, u, y, n, dtype, as_stream(stream));

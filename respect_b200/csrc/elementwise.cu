@@ -191,6 +191,98 @@ __global__ void silu_mul_f32_kernel(const float* __restrict__ g, const float* __
   }
 }
 
+// ------------------------------------------------------------------ prefill norms
+// respect/system/fused.py:126-194: the pieces of an eager RMSNorm (with the
+// residual add before it) whose bits PyTorch fixes elementwise, around the row
+// mean that PyTorch itself computes. add_sq: x = r + h in the promoted dtype
+// (rounded to bf16 when that is bf16), sq = x * x in fp32; with h == nullptr,
+// sq = r * r only. norm_apply: y = w * to_x_dtype(x * rsqrt(var + eps)) with
+// the output in promote(w, x) (rounded to bf16 when that is bf16).
+template <typename T>
+__device__ __forceinline__ float ld_f(const void* p, int64_t i) {
+  if constexpr (sizeof(T) == 2) return bf16_bits_to_f32(static_cast<const uint16_t*>(p)[i]);
+  else return static_cast<const float*>(p)[i];
+}
+template <typename T>
+__device__ __forceinline__ void st_f(void* p, int64_t i, float v) {
+  if constexpr (sizeof(T) == 2) static_cast<uint16_t*>(p)[i] = f32_to_bf16_bits(v);
+  else static_cast<float*>(p)[i] = v;
+}
+
+template <typename TR, typename TH, typename TX>
+__global__ void add_sq_kernel(const void* __restrict__ r, const void* __restrict__ h, void* __restrict__ x,
+                              float* __restrict__ sq, int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float v = ld_f<TR>(r, i);
+    if (h) {
+      v = __fadd_rn(v, ld_f<TH>(h, i));
+      if constexpr (sizeof(TX) == 2) v = round_bf16(v);
+      st_f<TX>(x, i, v);
+    }
+    sq[i] = __fmul_rn(v, v);
+  }
+}
+
+template <typename TX, typename TW, typename TY>
+__global__ void norm_apply_kernel(const void* __restrict__ x, const float* __restrict__ var, const void* __restrict__ w,
+                                  void* __restrict__ y, int64_t M, int N, float eps) {
+  const int64_t n = M * N;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / N;
+    const int col = static_cast<int>(i - row * N);
+    const float rs = rsqrtf(__fadd_rn(var[row], eps));
+    float xh = __fmul_rn(ld_f<TX>(x, i), rs);
+    if constexpr (sizeof(TX) == 2) xh = round_bf16(xh);
+    float v = __fmul_rn(ld_f<TW>(w, col), xh);
+    if constexpr (sizeof(TY) == 2) v = round_bf16(v);
+    st_f<TY>(y, i, v);
+  }
+}
+
+static unsigned ew_blocks(int64_t n) {
+  const int64_t b = (n + 255) / 256;
+  return static_cast<unsigned>(b < 148 * 32 ? (b < 1 ? 1 : b) : 148 * 32);
+}
+
+int add_sq_launch(const void* r, const void* h, void* x, float* sq, int64_t n, int tr, int th, int tx,
+                  cudaStream_t s) {
+  if (n <= 0) return RB_OK;
+  const unsigned g = ew_blocks(n);
+  // promote(r, h): bf16 only when both are bf16
+  const int want = h ? ((tr == RB_BF16 && th == RB_BF16) ? RB_BF16 : RB_F32) : tr;
+  if (h && tx != want) return RB_ERR_UNSUPPORTED;
+  if (!h) {
+    if (tr == RB_BF16) add_sq_kernel<uint16_t, uint16_t, uint16_t><<<g, 256, 0, s>>>(r, nullptr, nullptr, sq, n);
+    else add_sq_kernel<float, float, float><<<g, 256, 0, s>>>(r, nullptr, nullptr, sq, n);
+  } else if (tr == RB_BF16 && th == RB_BF16) {
+    add_sq_kernel<uint16_t, uint16_t, uint16_t><<<g, 256, 0, s>>>(r, h, x, sq, n);
+  } else if (tr == RB_BF16) {
+    add_sq_kernel<uint16_t, float, float><<<g, 256, 0, s>>>(r, h, x, sq, n);
+  } else if (th == RB_BF16) {
+    add_sq_kernel<float, uint16_t, float><<<g, 256, 0, s>>>(r, h, x, sq, n);
+  } else {
+    add_sq_kernel<float, float, float><<<g, 256, 0, s>>>(r, h, x, sq, n);
+  }
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;
+}
+
+int norm_apply_launch(const void* x, const float* var, const void* w, void* y, int64_t M, int N, float eps, int tx,
+                      int tw, int ty, cudaStream_t s) {
+  if (M <= 0) return RB_OK;
+  const int want = (tx == RB_BF16 && tw == RB_BF16) ? RB_BF16 : RB_F32;
+  if (ty != want) return RB_ERR_UNSUPPORTED;
+  const unsigned g = ew_blocks(M * N);
+#define RB_NORM_APPLY(A, B, C) norm_apply_kernel<A, B, C><<<g, 256, 0, s>>>(x, var, w, y, M, N, eps)
+  if (tx == RB_BF16 && tw == RB_BF16) RB_NORM_APPLY(uint16_t, uint16_t, uint16_t);
+  else if (tx == RB_BF16) RB_NORM_APPLY(uint16_t, float, float);
+  else if (tw == RB_BF16) RB_NORM_APPLY(float, uint16_t, float);
+  else RB_NORM_APPLY(float, float, float);
+#undef RB_NORM_APPLY
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;
+}
+
 int silu_mul_launch(const void* g, const void* u, void* y, int64_t n, int dtype, cudaStream_t s) {
   if (n <= 0) return RB_OK;
   if (dtype == RB_F32) {

@@ -275,6 +275,30 @@ def test_silu_mul_bitwise_vs_eager(dtype):
     assert torch.equal(silu_mul(a[:, :13], b[:, :13]), torch.nn.functional.silu(a[:, :13]) * b[:, :13])
 
 
+def _eager_rmsnorm(x, w, eps):
+    """HF Qwen3-VL RMSNorm forward."""
+    xf = x.float()
+    var = xf.pow(2).mean(-1, keepdim=True)
+    return w * (xf * torch.rsqrt(var + eps)).to(x.dtype)
+
+
+@pytest.mark.parametrize("rdt,hdt", [(torch.bfloat16, torch.bfloat16), (torch.float32, torch.float32),
+                                     (torch.bfloat16, torch.float32)])
+def test_prefill_add_sq_norm_bitwise_vs_eager(rdt, hdt):
+    """respect/system/fused.py:126-194: add_sq, norm_from, rmsnorm bit for bit with eager."""
+    from respect_b200.system.fused import add_sq, norm_from, rmsnorm
+    g = torch.Generator(device=DEV).manual_seed(8)
+    r = (torch.randn(300, 3584, device=DEV, generator=g) * 3).to(rdt)
+    h = torch.randn(300, 3584, device=DEV, generator=g).to(hdt)
+    w = (torch.rand(3584, device=DEV, generator=g) + 0.5).to(torch.bfloat16)
+    x, sq = add_sq(r, h)
+    assert torch.equal(x, r + h)
+    assert torch.equal(sq, (r + h).float() ** 2)
+    assert torch.equal(norm_from(x, sq, w, 1e-6), _eager_rmsnorm(r + h, w, 1e-6))
+    assert torch.equal(rmsnorm(x, w, 1e-6), _eager_rmsnorm(x, w, 1e-6))
+    assert torch.equal(rmsnorm(x, w.float(), 1e-6), _eager_rmsnorm(x, w.float(), 1e-6))
+
+
 # ---------------------------------------------------------------- decode helpers
 def test_greedy_token_matches_masked_argmax():
     from respect_b200.decoding.acceptance import greedy_token, mask_action_vocab
