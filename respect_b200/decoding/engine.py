@@ -160,19 +160,39 @@ class VerifyEngine:
     verify step writes its nodes after them.
     """
 
-    def __init__(self, weights: DecoderWeights, max_rows: int, max_slots: int, max_pos: int | None = None):
+    def __init__(self, weights: DecoderWeights, max_rows: int, max_slots: int | None = None,
+                 max_pos: int | None = None, kv=None):
+        """`kv`: a FixedKVBuffer (respect_b200.decoding.kv_buffer, allocated) whose per-layer
+        [1, Hkv, slots, D] bf16 tensors the engine uses as its KV buffer, so a Prefill written
+        into it (FixedKVBuffer.write_prefill) is verified in place; max_slots then defaults to
+        its slot count. Without it the engine allocates [Hkv, max_slots, D] per layer."""
         self.cfg = c = weights.cfg
         self.w = weights
         self.device = weights.embed.device
-        self.max_rows, self.max_slots = max_rows, max_slots
-        self.max_pos = max_pos or (max_slots + 1024)
         lib = _lib.lib()
         for n, (res, args) in _ENGINE_SIGS.items():
             fn = getattr(lib, n)
             fn.restype, fn.argtypes = res, args
-        self.kc = [torch.zeros(c.n_kv_heads, max_slots, c.head_dim, dtype=torch.bfloat16, device=self.device)
-                   for _ in range(c.n_layers)]
-        self.vc = [torch.zeros_like(k) for k in self.kc]
+        if kv is not None:
+            shape = (1, c.n_kv_heads, kv.base_k[0].shape[2], c.head_dim)
+            for t in list(kv.base_k) + list(kv.base_v):
+                if tuple(t.shape) != shape or t.dtype != torch.bfloat16 or not t.is_contiguous() or t.device != self.device:
+                    raise ValueError(f"KV buffer tensors must be contiguous bf16 {shape} on {self.device}")
+            if len(kv.base_k) != c.n_layers:
+                raise ValueError(f"KV buffer has {len(kv.base_k)} layers, the model {c.n_layers}")
+            max_slots = shape[2] if max_slots is None else max_slots
+            if max_slots > shape[2]:
+                raise ValueError(f"max_slots {max_slots} exceeds the buffer's {shape[2]} slots")
+            self.kc = [t[0] for t in kv.base_k]   # views: the engine writes the buffer in place
+            self.vc = [t[0] for t in kv.base_v]
+        else:
+            if max_slots is None:
+                raise ValueError("max_slots is required without a KV buffer")
+            self.kc = [torch.zeros(c.n_kv_heads, max_slots, c.head_dim, dtype=torch.bfloat16, device=self.device)
+                       for _ in range(c.n_layers)]
+            self.vc = [torch.zeros_like(k) for k in self.kc]
+        self.max_rows, self.max_slots = max_rows, max_slots
+        self.max_pos = max_pos or (max_slots + 1024)
         self.cos, self.sin = rope_table(self.max_pos, c.head_dim, c.rope_theta, self.device)
         self._cfg = _Cfg(c.hidden, c.n_layers, c.n_heads, c.n_kv_heads, c.head_dim, c.ffn, c.vocab,
                          c.rms_eps, max_rows, max_slots, self.max_pos)
@@ -203,6 +223,19 @@ class VerifyEngine:
         self._logits_ptr, self._ids_ptr, self._hidden_ptr = lg.value, ids.value, hid.value
         self._ids_host = torch.empty(max_rows, dtype=torch.int64, pin_memory=True)
         self.last_q = 0
+
+    def write_prefill(self, cache, prompt_len: int | None = None) -> None:
+        """Copy a Prefill cache (HF Cache or any object with .layers[i].keys / .values of shape
+        [1, Hkv, >= prompt_len, D]) into slots [0, prompt_len) (kv_buffer.py:66-71)."""
+        layers = cache.layers
+        if len(layers) != len(self.kc):
+            raise ValueError(f"cache has {len(layers)} layers, the engine {len(self.kc)}")
+        for k, v, layer in zip(self.kc, self.vc, layers):
+            pl = layer.keys.shape[2] if prompt_len is None else prompt_len
+            if pl > self.max_slots:
+                raise ValueError(f"prompt of {pl} tokens exceeds max_slots {self.max_slots}")
+            k[:, :pl].copy_(layer.keys[0, :, :pl])
+            v[:, :pl].copy_(layer.values[0, :, :pl])
 
     # ------------------------------------------------------------------ steps
     def step(self, ids, parents, depths, base: int, prompt_len: int, rope_delta: int = 0,

@@ -208,6 +208,50 @@ def test_device_accept_matches_host_walk(tiny):
     assert len(walk(tree, toks[0], 100, -1, lambda a, ch: int(ids[ch]))[0]) >= 10
 
 
+def test_engine_on_fixed_kv_buffer_and_prefill_write_in(tiny):
+    """The engine verifies in place on a FixedKVBuffer (kv_buffer.py:44-90) into which a
+    Prefill cache was written, and VerifyEngine.write_prefill copies the same cache into
+    an engine-owned buffer: both give the logits and node KV of the engine that prefilled
+    itself, bit for bit."""
+    from respect_b200.decoding.kv_buffer import FixedKVBuffer
+    cfg, w, eng = tiny
+    rng = np.random.default_rng(31)
+    P, CAP = 40, 192
+    eng.prefill(rng.integers(0, cfg.vocab, P))
+
+    class _Layer:
+        def __init__(self, k, v):
+            self.keys, self.values = k, v
+
+    class _Cache:
+        pass
+
+    cache = _Cache()   # the Prefill KV in HF's [1, Hkv, P, D] layout
+    cache.layers = [_Layer(k[:, :P].unsqueeze(0).clone(), v[:, :P].unsqueeze(0).clone())
+                    for k, v in zip(eng.kc, eng.vc)]
+    buf = FixedKVBuffer(P, (CAP,))
+    buf.allocate(cache)
+    buf.write_prefill(cache)
+    on_buf = VerifyEngine(w, max_rows=64, kv=buf)
+    own = VerifyEngine(w, max_rows=64, max_slots=P + CAP)
+    own.write_prefill(cache)
+    tree = build_trie(top_up(rng, chain_seqs(rng, 3, 10, cfg.vocab), 40, cfg.vocab))
+    args = (tree.tokens().astype(np.int32), tree.parents(), tree.depths(), 0, P)
+    q = len(tree.nodes)
+    try:
+        for e in (eng, on_buf, own):
+            e.step(*args)
+        for e in (on_buf, own):
+            assert torch.equal(e.logits(q), eng.logits(q))
+            for l in range(cfg.n_layers):
+                assert torch.equal(e.kc[l][:, :P + q], eng.kc[l][:, :P + q])
+                assert torch.equal(e.vc[l][:, :P + q], eng.vc[l][:, :P + q])
+        assert torch.equal(buf.base_k[0][0, :, P:P + q], eng.kc[0][:, P:P + q])   # written in place
+    finally:
+        on_buf.close()
+        own.close()
+
+
 @pytest.fixture(scope="module")
 def big():
     cfg = DecoderConfig.baseline_7b()
