@@ -161,11 +161,13 @@ class VerifyEngine:
     """
 
     def __init__(self, weights: DecoderWeights, max_rows: int, max_slots: int | None = None,
-                 max_pos: int | None = None, kv=None):
+                 max_pos: int | None = None, kv=None, share_weights: "VerifyEngine | None" = None):
         """`kv`: a FixedKVBuffer (respect_b200.decoding.kv_buffer, allocated) whose per-layer
         [1, Hkv, slots, D] bf16 tensors the engine uses as its KV buffer, so a Prefill written
         into it (FixedKVBuffer.write_prefill) is verified in place; max_slots then defaults to
-        its slot count. Without it the engine allocates [Hkv, max_slots, D] per layer."""
+        its slot count. Without it the engine allocates [Hkv, max_slots, D] per layer.
+        `share_weights`: another engine of the same model whose packed weights this one
+        reuses (several frame streams on one GPU hold the weights once)."""
         self.cfg = c = weights.cfg
         self.w = weights
         self.device = weights.embed.device
@@ -202,9 +204,14 @@ class VerifyEngine:
         self.ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
         # projection weights in the packed tile layout (gate|up with 256-row tiles)
         from respect_b200.kernels.gemm import pack_weight
-        self.packed = [dict(wqkv=pack_weight(lw["wqkv"]), wo=pack_weight(lw["wo"]), wgu=pack_weight(lw["wgu"], 256),
-                            wd=pack_weight(lw["wd"])) for lw in weights.layers]
-        self.lm_packed = pack_weight(weights.lm_head)
+        if share_weights is not None:
+            if share_weights.w is not weights:
+                raise ValueError("share_weights must be an engine of the same DecoderWeights")
+            self.packed, self.lm_packed = share_weights.packed, share_weights.lm_packed
+        else:
+            self.packed = [dict(wqkv=pack_weight(lw["wqkv"]), wo=pack_weight(lw["wo"]),
+                                wgu=pack_weight(lw["wgu"], 256), wd=pack_weight(lw["wd"])) for lw in weights.layers]
+            self.lm_packed = pack_weight(weights.lm_head)
         self._layers = (_LayerW * c.n_layers)(*[
             _LayerW(pk["wqkv"].data_ptr(), pk["wo"].data_ptr(), pk["wgu"].data_ptr(), pk["wd"].data_ptr(),
                     *(lw[k].data_ptr() for k in ("in_norm", "post_norm", "q_norm", "k_norm")))
