@@ -20,6 +20,11 @@ barrier and the max over ranks is reported.
 --impl reference: the reference's CPU path (the numpy oracle restating it,
 oracle/) on the host cores, on a bounded sample of the same step.
 
+--workload frame_replay [--streams S]: the multi-stream frame replay (S frame
+streams per GPU, 4,096-token prompts, 256-node tries, 80 committed tokens per
+frame); --warmup / --steps count frames per stream (defaults 1 / 2); metric
+frames/s.
+
 --kernel-case gemm_gate_up | attention: only that kernel at its config-3
 shape (--warmup untimed launches, then --steps timed ones), for profiling one
 kernel on a small footprint; prints one JSON line with the per-launch time.
@@ -54,13 +59,23 @@ KERNELS_FIXED = 3              # embed+norm, lm_head gemm (+ greedy keys), greed
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-case", default=None, choices=["gemm_gate_up", "attention"])
-    return ap.parse_args()
+    ap.add_argument("--workload", default="verify_step", choices=["verify_step", "frame_replay"])
+    ap.add_argument("--streams", type=int, default=16)
+    ap.add_argument("--nodes", type=int, default=NODES, help="verify_step: trie nodes (config 3: 128)")
+    ap.add_argument("--prefix", type=int, default=PROMPT, help="verify_step: prompt tokens (config 3: 3000)")
+    args = ap.parse_args()
+    replay = args.workload == "frame_replay" and not args.kernel_case
+    if args.steps is None:
+        args.steps = 2 if replay else 300
+    if args.warmup is None:
+        args.warmup = 1 if replay else 5
+    return args
 
 
 def measured_peaks():
@@ -83,10 +98,11 @@ def profiled_traffic():
     return None
 
 
-def config_block(n):
-    return {"workload": "config3: trie verify step, 28-layer 7B-class decoder, prefix 3000, 128-node trie",
+def config_block(n, nodes=NODES, prompt=PROMPT):
+    name = "config3: " if (nodes, prompt) == (NODES, PROMPT) else ""
+    return {"workload": f"{name}trie verify step, 28-layer 7B-class decoder, prefix {prompt}, {nodes}-node trie",
             "model": "qwen3-style random-init hidden3584 L28 H28/4 D128 F18944 V152064",
-            "prefix": PROMPT, "trie_nodes": NODES, "committed_per_step": CHAIN, "global_batch": n,
+            "prefix": prompt, "trie_nodes": nodes, "committed_per_step": CHAIN, "global_batch": n,
             "parallelism": f"replicas{n}", "l2": "inputs larger than L2 (14.1 GB weights per step)"}
 
 
@@ -213,6 +229,8 @@ class Clocks:
 # ------------------------------------------------------------------ native arm
 def run_native(args):
     import torch
+
+    NODES, PROMPT = args.nodes, args.prefix  # noqa: N806 (config 3: 128, 3000)
     import torch.distributed as dist
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -346,11 +364,99 @@ def run_native(args):
         line = {"metric": "committed tokens/s (trie-verify step)", "value": value, "unit": "committed tokens/s",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic (seeded ids, random-init weights)", "config": config_block(world),
+                "data": "synthetic (seeded ids, random-init weights)", "config": config_block(world, NODES, PROMPT),
                 "e2e": e2e, "gpu_launches": launches, "roofline": roof, "step_roofline": step_roof,
                 "cpu_baseline": cpu, "clocks": clocks, "device_error": err}
         print(json.dumps(line), flush=True)
     eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ frame replay
+def run_frame_replay(args):
+    """Multi-stream frame replay: --streams frame streams per GPU (16 by default),
+    each frame a 4,096-token prompt (90% shared with the previous frame, Prefill
+    reusing the unchanged chunks) and 256-node verification rounds until 80 tokens
+    are committed. --warmup frames per stream untimed, then --steps frames per
+    stream timed. Metric: frames/s (whole job)."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=dev)
+
+    from respect_b200 import _lib
+    from respect_b200.decoding.engine import DecoderConfig, DecoderWeights
+    from respect_b200.decoding.replay import FrameReplay, ReplayConfig
+
+    cfg = DecoderConfig.baseline_7b()
+    w = DecoderWeights.random(cfg, dev, seed=0)
+    rcfg = ReplayConfig(streams=args.streams, seed=1000 + rank)
+    rep = FrameReplay(w, rcfg)
+    warm = rep.run(args.warmup)
+    if world > 1:
+        dist.barrier()
+    with Clocks(local) as clk:
+        stats, ms = rep.timed_run(args.steps)
+    ms = reduce_max(ms, dev)
+    clocks = clk.summary()
+    frames = stats.frames
+    value = world * frames / (ms / 1e3)
+
+    # floor of the steps the timed frames ran (prefill chunks and verification
+    # rounds, 256 rows each): max(HBM bytes / peak, tensor FLOPs / peak) per step
+    hbm, tf, src = measured_peaks()
+    rows = rcfg.trie_nodes
+    keys = rcfg.prompt_len + rcfg.commit_tokens // 2 + rows // 2
+    kv_bytes = 2 * cfg.n_layers * 2 * cfg.n_kv_heads * keys * cfg.head_dim
+    step_bytes = cfg.weight_bytes_per_step() + kv_bytes + rows * cfg.vocab * 4
+    mm_flops = 2 * rows * (cfg.n_layers * cfg.layer_params() + cfg.vocab * cfg.hidden)
+    attn_flops = 4 * rows * cfg.n_layers * cfg.n_heads * cfg.head_dim * keys
+    t_hbm_ms = step_bytes / (hbm * 1e9) * 1e3
+    t_tc_ms = (mm_flops + attn_flops) / (tf * 1e12) * 1e3
+    n_steps = stats.rounds + stats.prefill_steps
+    floor_ms = n_steps * max(t_hbm_ms, t_tc_ms)
+    roof = {"bound": "hbm" if t_hbm_ms >= t_tc_ms else "tensor", "step_floor_ms": max(t_hbm_ms, t_tc_ms),
+            "unit": "ms", "floor_ms": floor_ms, "achieved_ms": ms, "frac": floor_ms / ms,
+            "peak_hbm_gbs": hbm, "peak_tflops": tf, "peak_source": src,
+            "step_bytes": step_bytes, "step_flops": mm_flops + attn_flops, "steps": n_steps,
+            "traffic": None}
+    per_round = 32 + 3 * 4 * rows
+    h2d = (stats.prefill_tokens * 12 + stats.prefill_steps * 32 + stats.rounds * per_round) / max(frames, 1)
+    d2h = (stats.rounds * 4 * (4 + 2 * rows) + frames * 8 * rcfg.prefill_chunk) / max(frames, 1)
+    err = _lib.device_error()
+    if rank == 0:
+        line = {"metric": "frames/s (multi-stream frame replay)", "value": value, "unit": "frames/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (seeded prompts and edits, random-init weights)",
+                "config": {"workload": "frame replay: 28-layer 7B-class decoder, 4096-token prompts 90% shared "
+                                       "with the previous frame, 256-node tries (4 chains of 48 + continuation "
+                                       "nodes), 80 committed tokens per frame",
+                           "streams_per_gpu": rcfg.streams, "frames_per_stream": args.steps,
+                           "parallelism": f"replicas{world}",
+                           "l2": "inputs larger than L2 (14.1 GB weights per step)"},
+                "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                        "path": "FrameReplay.run: host prompts -> VerifyEngine.prefill, host tries -> "
+                                "VerifyEngine.step, device acceptance record -> host; the timed region is "
+                                "end to end (bytes per frame)"},
+                "gpu_launches": n_steps * (KERNELS_FIXED + KERNELS_PER_LAYER * cfg.n_layers) + stats.rounds * 2,
+                "roofline": roof, "cpu_baseline": None,
+                "replay": {"frames": frames, "rounds": stats.rounds, "committed": stats.committed,
+                           "tokens_per_round": stats.tokens_per_round(), "prefill_steps": stats.prefill_steps,
+                           "prefill_tokens_per_frame": stats.prefill_tokens / max(frames, 1),
+                           "warmup_frames": warm.frames},
+                "clocks": clocks, "device_error": err}
+        print(json.dumps(line), flush=True)
+    rep.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -414,6 +520,8 @@ def main():
         run_kernel_case(args)
     elif args.impl == "reference":
         run_reference(args)
+    elif args.workload == "frame_replay":
+        run_frame_replay(args)
     else:
         run_native(args)
 

@@ -74,12 +74,13 @@ def verify_step(W, cfg, ids, parents, depths, prompt_len, base, kc, vc, bf16=Tru
 
 
 def prefill(W, cfg, tokens, kc, vc, chunk=64, bf16=True):
-    """Prompt KV by chained steps (prompt_len 0, each chunk a chain after the previous ones)."""
+    """Prompt KV by chained steps: chunk c is a chain whose prompt is the c * chunk
+    tokens before it (prompt_len c * chunk, base 0)."""
     toks = np.asarray(tokens)
     for s in range(0, len(toks), chunk):
         part = toks[s:s + chunk]
         n = len(part)
-        verify_step(W, cfg, part, np.arange(-1, n - 1), np.arange(n), 0, s, kc, vc, bf16=bf16)
+        verify_step(W, cfg, part, np.arange(-1, n - 1), np.arange(n), s, 0, kc, vc, bf16=bf16)
 
 
 def weights_from_engine(w, cfg):

@@ -414,11 +414,14 @@ struct rb_engine {
   CUtensorMap m_xn, m_attn, m_act, m_lm;
   std::vector<CUtensorMap> m_qkv, m_o, m_gu, m_d, m_kc, m_vc;
   int bn_lm = 256;
-  // host staging and graphs
+  // host staging (a ring of pinned slots, so a host that enqueues many steps ahead,
+  // a chunked prefill, waits only for the copy kStageSlots steps back) and graphs
+  static constexpr int kStageSlots = 32;
   uint8_t* pinned = nullptr;
-  size_t pinned_bytes = 0;
-  cudaEvent_t staged = nullptr;
-  bool staged_pending = false;
+  size_t slot_bytes = 0;
+  cudaEvent_t staged[kStageSlots] = {};
+  bool staged_pending[kStageSlots] = {};
+  int next_slot = 0;
   cudaStream_t cap = nullptr;
   std::map<int, cudaGraphExec_t> graphs;
   std::map<int, cudaGraph_t> graph_defs;
@@ -718,10 +721,12 @@ int rb_engine_create(const rb_model_config* cfg, const rb_model_weights* w, void
     delete e;
     return RB_ERR_CUDA;
   }
-  e->pinned_bytes = sizeof(StepParams) + 3 * static_cast<size_t>(c.max_rows) * 4;
-  if (cudaMallocHost(&e->pinned, e->pinned_bytes) != cudaSuccess ||
-      cudaEventCreateWithFlags(&e->staged, cudaEventDisableTiming) != cudaSuccess ||
-      cudaStreamCreateWithFlags(&e->cap, cudaStreamNonBlocking) != cudaSuccess) {
+  e->slot_bytes = align256(sizeof(StepParams) + 3 * static_cast<size_t>(c.max_rows) * 4);
+  bool ok = cudaMallocHost(&e->pinned, e->slot_bytes * rb_engine::kStageSlots) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&e->cap, cudaStreamNonBlocking) == cudaSuccess;
+  for (int i = 0; ok && i < rb_engine::kStageSlots; ++i)
+    ok = cudaEventCreateWithFlags(&e->staged[i], cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) {
     rb_engine_destroy(e);
     return RB_ERR_CUDA;
   }
@@ -733,7 +738,8 @@ int rb_engine_destroy(rb_engine* e) {
   if (!e) return RB_OK;
   for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
   for (auto& kv : e->graph_defs) cudaGraphDestroy(kv.second);
-  if (e->staged) cudaEventDestroy(e->staged);
+  for (int i = 0; i < rb_engine::kStageSlots; ++i)
+    if (e->staged[i]) cudaEventDestroy(e->staged[i]);
   if (e->cap) cudaStreamDestroy(e->cap);
   if (e->pinned) cudaFreeHost(e->pinned);
   delete e;
@@ -764,38 +770,34 @@ int rb_engine_step(rb_engine* e, const rb_step_desc* d, void* stream) {
       if (d->depths[i] != (p < 0 ? 0 : d->depths[p] + 1)) return RB_ERR_INVALID_ARG;
       if (d->ids[i] < 0 || d->ids[i] >= c.vocab) return RB_ERR_INVALID_ARG;
     }
-    if (e->staged_pending) {
-      if (cudaEventSynchronize(e->staged) != cudaSuccess) return RB_ERR_CUDA;
-      e->staged_pending = false;
-    }
-    uint8_t* p = e->pinned;
-    memcpy(p, &sp, sizeof(sp));
+  }
+  const int slot = e->next_slot;
+  e->next_slot = (slot + 1) % rb_engine::kStageSlots;
+  if (e->staged_pending[slot]) {  // this slot's previous copy must have left the pinned buffer
+    if (cudaEventSynchronize(e->staged[slot]) != cudaSuccess) return RB_ERR_CUDA;
+    e->staged_pending[slot] = false;
+  }
+  uint8_t* p = e->pinned + static_cast<size_t>(slot) * e->slot_bytes;
+  memcpy(p, &sp, sizeof(sp));
+  if (cudaMemcpyAsync(e->d_params, p, sizeof(sp), cudaMemcpyHostToDevice, st) != cudaSuccess) return RB_ERR_CUDA;
+  if (d->host_inputs) {
+    // params, ids, parents, depths are laid out back to back in the workspace
+    // only up to alignment, so copy each piece to its place.
     memcpy(p + sizeof(sp), d->ids, n4);
     memcpy(p + sizeof(sp) + n4, d->parents, n4);
     memcpy(p + sizeof(sp) + 2 * n4, d->depths, n4);
-    // params, ids, parents, depths are laid out back to back in the workspace
-    // only up to alignment, so copy each piece to its place.
-    if (cudaMemcpyAsync(e->d_params, p, sizeof(sp), cudaMemcpyHostToDevice, st) != cudaSuccess ||
-        cudaMemcpyAsync(e->d_ids, p + sizeof(sp), n4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+    if (cudaMemcpyAsync(e->d_ids, p + sizeof(sp), n4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
         cudaMemcpyAsync(e->d_parents, p + sizeof(sp) + n4, n4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-        cudaMemcpyAsync(e->d_depths, p + sizeof(sp) + 2 * n4, n4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-        cudaEventRecord(e->staged, st) != cudaSuccess)
+        cudaMemcpyAsync(e->d_depths, p + sizeof(sp) + 2 * n4, n4, cudaMemcpyHostToDevice, st) != cudaSuccess)
       return RB_ERR_CUDA;
-    e->staged_pending = true;
   } else {
-    if (e->staged_pending) {
-      if (cudaEventSynchronize(e->staged) != cudaSuccess) return RB_ERR_CUDA;
-      e->staged_pending = false;
-    }
-    memcpy(e->pinned, &sp, sizeof(sp));
-    if (cudaMemcpyAsync(e->d_params, e->pinned, sizeof(sp), cudaMemcpyHostToDevice, st) != cudaSuccess ||
-        cudaMemcpyAsync(e->d_ids, d->ids, n4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+    if (cudaMemcpyAsync(e->d_ids, d->ids, n4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
         cudaMemcpyAsync(e->d_parents, d->parents, n4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
-        cudaMemcpyAsync(e->d_depths, d->depths, n4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
-        cudaEventRecord(e->staged, st) != cudaSuccess)
+        cudaMemcpyAsync(e->d_depths, d->depths, n4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
       return RB_ERR_CUDA;
-    e->staged_pending = true;
   }
+  if (cudaEventRecord(e->staged[slot], st) != cudaSuccess) return RB_ERR_CUDA;
+  e->staged_pending[slot] = true;
   const int rows = std::min(bucket_of(d->q), c.max_rows);  // workspace holds max_rows rows
   if (!d->use_graph) return enqueue_step(e, rows, st);
   auto it = e->graphs.find(rows);

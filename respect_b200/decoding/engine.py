@@ -229,6 +229,11 @@ class VerifyEngine:
         _lib.call("rb_engine_outputs", h, ctypes.byref(lg), ctypes.byref(ids), ctypes.byref(hid), None)
         self._logits_ptr, self._ids_ptr, self._hidden_ptr = lg.value, ids.value, hid.value
         self._ids_host = torch.empty(max_rows, dtype=torch.int64, pin_memory=True)
+        self._rec_host = torch.empty(4 + 2 * max_rows, dtype=torch.int32, pin_memory=True)
+        self._rec_event = torch.cuda.Event()
+        self._rec_n = 0
+        self._ids_event = torch.cuda.Event()
+        self._ids_n = 0
         self.last_q = 0
 
     def write_prefill(self, cache, prompt_len: int | None = None) -> None:
@@ -285,6 +290,18 @@ class VerifyEngine:
         st.synchronize()
         return self._ids_host[:q].numpy()
 
+    def fetch_ids_async(self, q: int | None = None, stream=None) -> None:
+        """Enqueue the copy of the last step's greedy ids to the host; ids_result() waits for it."""
+        q = self.last_q if q is None else q
+        st = stream or torch.cuda.current_stream(self.device)
+        _lib.call("rb_engine_fetch_ids", self._h, self._ids_host.data_ptr(), q, st.cuda_stream)
+        self._ids_event.record(st)
+        self._ids_n = q
+
+    def ids_result(self) -> np.ndarray:
+        self._ids_event.synchronize()
+        return self._ids_host[:self._ids_n].numpy().copy()
+
     def compact(self, path, prompt_len: int, base: int, stream=None) -> None:
         """Move the accepted path's KV to consecutive slots (kv_buffer.py:93-104)."""
         if not len(path):
@@ -299,13 +316,27 @@ class VerifyEngine:
         (rb_engine_accept): returns (path, tokens, correction) like
         respect_b200.decoding.acceptance.walk, with the accepted KV already moved to
         prompt_len + base + i. n bounds the record read back (default: max_rows)."""
+        self.accept_async(first, cap, eos, n, stream)
+        return self.accept_result()
+
+    def accept_async(self, first: int, cap: int, eos: int, n: int | None = None, stream=None) -> None:
+        """Enqueue the walk, the compaction and the record's copy to the host; the host does
+        not wait (several frame streams keep the device busy meanwhile). accept_result()
+        waits for the record."""
         st = stream or torch.cuda.current_stream(self.device)
         n = self.max_rows if n is None else n
+        if not 0 <= n <= self.max_rows:
+            raise ValueError(f"n={n} outside [0, {self.max_rows}]")
         _lib.call("rb_engine_accept", self._h, int(first), int(cap), int(eos), st.cuda_stream)
-        rec = torch.empty(4 + 2 * n, dtype=torch.int32, pin_memory=True)
-        _lib.call("rb_engine_fetch_accept", self._h, rec.data_ptr(), n, st.cuda_stream)
-        st.synchronize()
-        r = rec.tolist()
+        _lib.call("rb_engine_fetch_accept", self._h, self._rec_host.data_ptr(), n, st.cuda_stream)
+        self._rec_event.record(st)
+        self._rec_n = n
+
+    def accept_result(self):
+        """(path, tokens, correction) of the last accept_async, after its copy has landed."""
+        self._rec_event.synchronize()
+        n = self._rec_n
+        r = self._rec_host[:4 + 2 * n].tolist()
         cnt = r[0]
         return r[4:4 + cnt], r[4 + n:4 + n + cnt], r[1]
 
@@ -316,16 +347,35 @@ class VerifyEngine:
                   act_off=act_off, act_size=act_size, graph=graph)
         return self.fetch_ids(len(tree.nodes))
 
-    def prefill(self, tokens, chunk: int | None = None, graph: bool = True) -> None:
-        """Fill KV slots [0, len(tokens)) by running the prompt as chained steps
-        (prompt_len 0, each chunk a linear chain after the previous chunks)."""
+    def prefill(self, tokens, chunk: int | None = None, graph: bool = True, reuse=None, stream=None) -> int:
+        """Fill KV slots [0, len(tokens)) by running the prompt in chunks: chunk c is a
+        linear chain whose prompt is the c * chunk tokens before it (prompt_len = c * chunk,
+        base 0), so the earlier chunks are read by the prefix phase of the attention.
+
+        `reuse`: the tokens whose KV the buffer holds now (the previous frame's prompt,
+        prefilled with the same chunk). The chunks that lie entirely before the first
+        token that differs are kept: a slot's KV depends only on the tokens up to it and
+        the chunk grid, so the kept slots equal a recompute bitwise. Returns the number
+        of tokens recomputed (at least the last chunk, whose last row's greedy pick, in
+        next_ids(), is the token after the prompt)."""
         chunk = chunk or self.max_rows
         toks = np.asarray(tokens, np.int32)
-        for s in range(0, len(toks), chunk):
+        if len(toks) > self.max_slots:
+            raise ValueError(f"prompt of {len(toks)} tokens exceeds max_slots {self.max_slots}")
+        start = 0
+        if reuse is not None:
+            old = np.asarray(reuse, np.int32)
+            n = min(len(old), len(toks))
+            diff = np.flatnonzero(old[:n] != toks[:n])
+            lcp = int(diff[0]) if len(diff) else n
+            # the last chunk always runs: its last row's greedy pick is the first token
+            start = min((lcp // chunk) * chunk, ((len(toks) - 1) // chunk) * chunk)
+        for s in range(start, len(toks), chunk):
             part = toks[s:s + chunk]
             n = len(part)
-            self.step(part, np.arange(-1, n - 1, dtype=np.int32), np.arange(n, dtype=np.int32), s, 0,
-                      graph=graph)
+            self.step(part, np.arange(-1, n - 1, dtype=np.int32), np.arange(n, dtype=np.int32), 0, s,
+                      graph=graph, stream=stream)
+        return len(toks) - start
 
     def close(self) -> None:
         if getattr(self, "_h", None):
