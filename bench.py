@@ -468,6 +468,7 @@ def run_kernel_case(args):
     from respect_b200.decoding.engine import DecoderConfig
     dev = torch.device("cuda", 0)
     cfg = DecoderConfig.baseline_7b()
+    NODES, PROMPT = args.nodes, args.prefix  # noqa: N806 (config 3: 128, 3000)
     g = torch.Generator(device=dev).manual_seed(7)
     st = torch.cuda.current_stream(dev)
     if args.kernel_case == "gemm_gate_up":
@@ -484,6 +485,7 @@ def run_kernel_case(args):
         def launch(i):
             linear_swiglu_packed(x, ws[i % 2], F)
         algo = 2 * F * h * 2 + NODES * h * 2 + NODES * F * 2
+        flops = 2 * NODES * 2 * F * h
     else:
         from respect_b200.kernels.attention import fused_attn_hyb
         from oracle.trie import ancestry
@@ -500,6 +502,7 @@ def run_kernel_case(args):
         def launch(i):
             fused_attn_hyb(q, kp, vp, kn, vn, msk)
         algo = 2 * HK * (PROMPT + NODES) * D * 2 + 2 * H * NODES * D * 2
+        flops = 4 * H * NODES * PROMPT * D
     for i in range(args.warmup):
         launch(i)
     torch.cuda.synchronize()
@@ -511,7 +514,8 @@ def run_kernel_case(args):
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / args.steps
     print(json.dumps({"kernel_case": args.kernel_case, "launches": args.steps, "us_per_launch": us,
-                      "algorithmic_bytes": algo, "GBps": algo / (us * 1e-6) / 1e9}), flush=True)
+                      "rows": NODES, "algorithmic_bytes": algo, "GBps": algo / (us * 1e-6) / 1e9,
+                      "tensor_flops": flops, "TFLOPs": flops / (us * 1e-6) / 1e12}), flush=True)
 
 
 def main():

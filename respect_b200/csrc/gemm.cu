@@ -26,7 +26,10 @@ template <int BN, int MT>
 struct GemmCfg {
   static constexpr int kWTileBytes = BN * kBK * 2;
   static constexpr int kXStageBytes = MT * kXTileBytes;
-  static constexpr int kXStages = 2;
+  // Two token tiles per stage (256 rows) take as long in the tensor pipe as a
+  // weight tile takes to arrive; a third token stage keeps their L2 round trip
+  // (issued only when a stage is released) off the MMA's path.
+  static constexpr int kXStages = MT == 2 ? 3 : 2;
   static constexpr int kWStagesRaw = (kSmemLimit - 1024 - 256 - kXStages * kXStageBytes) / kWTileBytes;
   static constexpr int kWStages = kWStagesRaw > 8 ? 8 : kWStagesRaw;
   static constexpr int kWOff = 0;
