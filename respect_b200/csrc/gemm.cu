@@ -21,8 +21,8 @@ __host__ __device__ constexpr int pow2_cols(int c) {
 }
 
 // Shared memory: a ring of weight tiles (BN x 64, the DRAM stream, as deep as
-// fits) and a short ring of token tiles (MT x 128 x 64, L2-resident).
-template <int BN, int MT>
+// fits, at most WMAX) and a short ring of token tiles (MT x 128 x 64, L2-resident).
+template <int BN, int MT, int WMAX = 8>
 struct GemmCfg {
   static constexpr int kWTileBytes = BN * kBK * 2;
   static constexpr int kXStageBytes = MT * kXTileBytes;
@@ -31,7 +31,7 @@ struct GemmCfg {
   // (issued only when a stage is released) off the MMA's path.
   static constexpr int kXStages = MT == 2 ? 3 : 2;
   static constexpr int kWStagesRaw = (kSmemLimit - 1024 - 256 - kXStages * kXStageBytes) / kWTileBytes;
-  static constexpr int kWStages = kWStagesRaw > 8 ? 8 : kWStagesRaw;
+  static constexpr int kWStages = kWStagesRaw > WMAX ? WMAX : kWStagesRaw;
   static constexpr int kWOff = 0;
   static constexpr int kXOff = kWStages * kWTileBytes;
   static constexpr int kBarOff = kXOff + kXStages * kXStageBytes;
@@ -60,6 +60,16 @@ __host__ __device__ constexpr int gemm_stage_row_bytes(int epi, int bn) {
          : ((epi == kEpiSiluMul ? bn / 2 : bn) * gemm_out_elem_bytes(epi)) % 128 == 0 ? 128
          : ((epi == kEpiSiluMul ? bn / 2 : bn) * gemm_out_elem_bytes(epi)) % 64 == 0 ? 64
                                                                                      : 0;
+}
+
+// Weight-ring cap by epilogue. The fp32 outputs are the vocabulary projection,
+// whose grid runs several CTAs per SM one after another: with three weight
+// stages a CTA needs 111 KB of shared memory (BN = 208), so two share an SM and
+// one's prologue and epilogue overlap the other's weight stream. The
+// single-wave grids, and CTAs with two token tiles (which do not fit twice
+// anyway), keep the deep ring.
+__host__ __device__ constexpr int gemm_w_stage_cap(int epi, int mt) {
+  return (mt == 1 && (epi == kEpiStoreF32 || epi == kEpiF32Argmax)) ? 3 : 8;
 }
 
 struct GemmKernelArgs {
@@ -140,7 +150,7 @@ template <int BN, int MT, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
                 const __grid_constant__ CUtensorMap tmo, const GemmKernelArgs a) {
-  using C = GemmCfg<BN, MT>;
+  using C = GemmCfg<BN, MT, gemm_w_stage_cap(EPI, MT)>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
@@ -491,9 +501,13 @@ int gemm_pack_weight(const void* w, int64_t ldw, int N, int K, int BN, void* out
 template <int BN, int MT, int EPI>
 static int launch_t(const GemmShape& s, const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& mo,
                     const GemmKernelArgs& ka, cudaStream_t stream, bool pdl) {
-  using C = GemmCfg<BN, MT>;
+  using C = GemmCfg<BN, MT, gemm_w_stage_cap(EPI, MT)>;
   auto kern = gemm_kernel<BN, MT, EPI>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
+    return RB_ERR_CUDA;
+  // all of the unified L1 / shared memory as shared: two capped-ring CTAs per SM
+  if (gemm_w_stage_cap(EPI, MT) < 8 &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
     return RB_ERR_CUDA;
   dim3 grid(s.n_tiles, s.splits, s.m_groups);
   return launch_k(kern, grid, dim3(kGemmThreads), C::kSmemBytes, stream, pdl, mx, mw, mo, ka);
