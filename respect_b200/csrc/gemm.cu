@@ -22,14 +22,17 @@ __host__ __device__ constexpr int pow2_cols(int c) {
 
 // Shared memory: a ring of weight tiles (BN x 64, the DRAM stream, as deep as
 // fits, at most WMAX) and a short ring of token tiles (MT x 128 x 64, L2-resident).
-template <int BN, int MT, int WMAX = 8>
+template <int BN, int MT, int WMAX = 12>
 struct GemmCfg {
   static constexpr int kWTileBytes = BN * kBK * 2;
   static constexpr int kXStageBytes = MT * kXTileBytes;
   // Two token tiles per stage (256 rows) take as long in the tensor pipe as a
   // weight tile takes to arrive; a third token stage keeps their L2 round trip
   // (issued only when a stage is released) off the MMA's path.
-  static constexpr int kXStages = MT == 2 ? 3 : 2;
+  // 128-wide weight tiles (the short q|k|v and o projections) run their main
+  // loop only once the previous kernel ends, with most of their weights already
+  // in the ring: four token stages keep the token tiles' L2 round trips apart.
+  static constexpr int kXStages = MT == 2 ? 3 : (BN <= 128 ? 4 : 2);
   static constexpr int kWStagesRaw = (kSmemLimit - 1024 - 256 - kXStages * kXStageBytes) / kWTileBytes;
   static constexpr int kWStages = kWStagesRaw > WMAX ? WMAX : kWStagesRaw;
   static constexpr int kWOff = 0;
@@ -43,6 +46,7 @@ struct GemmCfg {
   static_assert(kWStages >= 3, "weight ring needs three stages");
   static_assert(kWTileBytes % 1024 == 0 && kXTileBytes % 1024 == 0, "swizzle atoms are 1024-byte aligned");
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
+  static_assert((2 * kWStages + 2 * kXStages + 1) * 8 + 4 <= 256, "barriers and TMEM slot fit their 256 bytes");
 };
 
 // Output element size of an epilogue, and the row width in bytes of the
@@ -69,7 +73,7 @@ __host__ __device__ constexpr int gemm_stage_row_bytes(int epi, int bn) {
 // single-wave grids, and CTAs with two token tiles (which do not fit twice
 // anyway), keep the deep ring.
 __host__ __device__ constexpr int gemm_w_stage_cap(int epi, int mt) {
-  return (mt == 1 && (epi == kEpiStoreF32 || epi == kEpiF32Argmax)) ? 3 : 8;
+  return (mt == 1 && (epi == kEpiStoreF32 || epi == kEpiF32Argmax)) ? 3 : 12;
 }
 
 struct GemmKernelArgs {
@@ -506,7 +510,7 @@ static int launch_t(const GemmShape& s, const CUtensorMap& mx, const CUtensorMap
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
     return RB_ERR_CUDA;
   // all of the unified L1 / shared memory as shared: two capped-ring CTAs per SM
-  if (gemm_w_stage_cap(EPI, MT) < 8 &&
+  if (gemm_w_stage_cap(EPI, MT) < 12 &&
       cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
     return RB_ERR_CUDA;
   dim3 grid(s.n_tiles, s.splits, s.m_groups);
