@@ -124,9 +124,9 @@ def job_value(world: int, units_per_step: float, steps: int, ms: float) -> float
 
 
 # ------------------------------------------------------------------ CPU sample (oracle)
-def cpu_sample(steps, warmup, seed=0):
-    """One decoder layer of the step (128 rows vs the 3000-token prefix) plus 1/28
-    of the lm_head rows, in the numpy oracle; a step is 28 such samples."""
+def cpu_sample(steps, warmup, seed=0, nodes=NODES, prompt=PROMPT, chain=CHAIN):
+    """One decoder layer of the step (`nodes` rows vs the `prompt`-token prefix; config 3:
+    128 vs 3000) plus 1/28 of the lm_head rows, in the numpy oracle; a step is 28 such samples."""
     from oracle import model as omodel
     from oracle.bf16 import round_bf16
     from oracle.inputs import chain_seqs, top_up
@@ -141,9 +141,9 @@ def cpu_sample(steps, warmup, seed=0):
               q_norm=np.ones(D, np.float32), k_norm=np.ones(D, np.float32))
     W = dict(embed=nrm(V // 28, h), lm_head=nrm(V // 28, h), final_norm=np.ones(h, np.float32), layers=[lw])
     cfg = dict(n_heads=H, n_kv_heads=HK, head_dim=D, rms_eps=1e-6, rope_theta=1e6)
-    tree = build_trie(top_up(rng, chain_seqs(rng, 4, CHAIN, V // 28), NODES, V // 28))
-    kc = [round_bf16(rng.standard_normal((HK, PROMPT + NODES, D), dtype=np.float32))]
-    vc = [round_bf16(rng.standard_normal((HK, PROMPT + NODES, D), dtype=np.float32))]
+    tree = build_trie(top_up(rng, chain_seqs(rng, 4, chain, V // 28), nodes, V // 28))
+    kc = [round_bf16(rng.standard_normal((HK, prompt + nodes, D), dtype=np.float32))]
+    vc = [round_bf16(rng.standard_normal((HK, prompt + nodes, D), dtype=np.float32))]
     # all host threads (torchrun sets OMP_NUM_THREADS=1 for its workers; the
     # BLAS pool is raised explicitly and the count actually in use reported)
     from threadpoolctl import threadpool_info, threadpool_limits
@@ -152,14 +152,14 @@ def cpu_sample(steps, warmup, seed=0):
         pools = [p["num_threads"] for p in threadpool_info()]
         for i in range(warmup + steps):
             t0 = time.perf_counter()
-            omodel.verify_step(W, cfg, tree.tokens(), tree.parents(), tree.depths(), PROMPT, 0, kc, vc)
+            omodel.verify_step(W, cfg, tree.tokens(), tree.parents(), tree.depths(), prompt, 0, kc, vc)
             if i >= warmup:
                 times.append(time.perf_counter() - t0)
     t_step = 28 * statistics.median(times)
     threads = max(pools) if pools else 1
-    return dict(value=CHAIN / t_step, unit="committed tokens/s", cores=threads, kind="port",
-                sample=("numpy oracle (oracle/model.py), one full-size decoder layer of the config-3 step "
-                        "(128 trie rows vs a 3000-token prefix) plus 1/28 of the lm_head rows; "
+    return dict(value=chain / t_step, unit="committed tokens/s", cores=threads, kind="port",
+                sample=("numpy oracle (oracle/model.py), one full-size decoder layer of the verify step "
+                        f"({nodes} trie rows vs a {prompt}-token prefix) plus 1/28 of the lm_head rows; "
                         f"step time = 28 x median of {steps} samples = {t_step:.2f} s"),
                 ms_per_step=t_step * 1e3)
 
@@ -356,7 +356,7 @@ def run_native(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cb = cpu_sample(2, 1)
+        cb = cpu_sample(2, 1, nodes=NODES, prompt=PROMPT)
         cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
     err = _lib.device_error()
     launches = args.steps * (KERNELS_FIXED + KERNELS_PER_LAYER * cfg.n_layers)
@@ -432,6 +432,15 @@ def run_frame_replay(args):
     per_round = 32 + 3 * 4 * rows
     h2d = (stats.prefill_tokens * 12 + stats.prefill_steps * 32 + stats.rounds * per_round) / max(frames, 1)
     d2h = (stats.rounds * 4 * (4 + 2 * rows) + frames * 8 * rcfg.prefill_chunk) / max(frames, 1)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # the oracle's 256-row step at the 4096-token prefix, times the steps the timed
+        # frames ran (prefill chunks counted as full-prefix steps: an upper bound)
+        cb = cpu_sample(2, 1, nodes=rows, prompt=rcfg.prompt_len, chain=rcfg.chain_len)
+        cpu_frame_s = n_steps * cb["ms_per_step"] / 1e3 / max(frames, 1)
+        cpu = {"value": 1.0 / cpu_frame_s, "unit": "frames/s", "cores": cb["cores"], "kind": "port",
+               "sample": cb["sample"] + f"; a frame = {n_steps / max(frames, 1):.1f} such steps (the timed "
+                         f"frames' prefill chunks and rounds) = {cpu_frame_s:.0f} s"}
     err = _lib.device_error()
     if rank == 0:
         line = {"metric": "frames/s (multi-stream frame replay)", "value": value, "unit": "frames/s",
@@ -449,7 +458,7 @@ def run_frame_replay(args):
                                 "VerifyEngine.step, device acceptance record -> host; the timed region is "
                                 "end to end (bytes per frame)"},
                 "gpu_launches": n_steps * (KERNELS_FIXED + KERNELS_PER_LAYER * cfg.n_layers) + stats.rounds * 2,
-                "roofline": roof, "cpu_baseline": None,
+                "roofline": roof, "cpu_baseline": cpu,
                 "replay": {"frames": frames, "rounds": stats.rounds, "committed": stats.committed,
                            "tokens_per_round": stats.tokens_per_round(), "prefill_steps": stats.prefill_steps,
                            "prefill_tokens_per_frame": stats.prefill_tokens / max(frames, 1),
