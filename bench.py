@@ -25,6 +25,11 @@ streams per GPU, 4,096-token prompts, 256-node tries, 80 committed tokens per
 frame); --warmup / --steps count frames per stream (defaults 1 / 2); metric
 frames/s.
 
+--kernel-case config1 | config2: the standalone operators of configs 1 and 2
+(fp32 trie attention; RMSNorm, RoPE, SiLU*mul) at their BASELINE shapes, timed per
+launch after an L2 flush, next to PyTorch eager on the host cores; one JSON line
+per operator.
+
 --kernel-case gemm_gate_up | attention: only that kernel at its config-3
 shape (--warmup untimed launches, then --steps timed ones), for profiling one
 kernel on a small footprint; prints one JSON line with the per-launch time.
@@ -64,7 +69,7 @@ def parse():
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel-case", default=None, choices=["gemm_gate_up", "attention"])
+    ap.add_argument("--kernel-case", default=None, choices=["gemm_gate_up", "attention", "config1", "config2"])
     ap.add_argument("--workload", default="verify_step", choices=["verify_step", "frame_replay"])
     ap.add_argument("--streams", type=int, default=16)
     ap.add_argument("--nodes", type=int, default=NODES, help="verify_step: trie nodes (config 3: 128)")
@@ -472,6 +477,127 @@ def run_frame_replay(args):
 
 
 # ------------------------------------------------------------------ single-kernel cases
+def _median_launch_us(torch, fn, reps, flush):
+    """Median device time of fn() over `reps` launches, each preceded by an L2 flush
+    (a write of a buffer larger than L2) and bracketed by CUDA events. fn is captured
+    in a CUDA graph first, so the host's wrapper work stays out of the timed region."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    ts = []
+    for _ in range(reps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    return statistics.median(ts)
+
+
+def _median_cpu_ms(fn, reps):
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        fn()
+        ts.append((time.perf_counter() - t0) * 1e3)
+    return statistics.median(ts)
+
+
+def run_config_case(args):
+    """Configs 1 and 2: the standalone operators at their BASELINE shapes, timed per
+    launch after an L2 flush (their inputs fit in L2), next to PyTorch eager on the
+    host cores at the same shapes (the reference's CPU path for these operators)."""
+    import torch
+    dev = torch.device("cuda", 0)
+    hbm, _, src = measured_peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    reps, warm = max(args.steps, 20), max(args.warmup, 3)
+    threads = torch.get_num_threads()
+    lines = []
+    if args.kernel_case == "config1":
+        from oracle.inputs import attention_case
+        from respect_b200.kernels.attention import fused_attn_hyb
+        c = attention_case(0)
+        t = {k: torch.from_numpy(np.ascontiguousarray(c[k])) for k in ("q", "kp", "vp", "kn", "vn", "msk")}
+        g = {k: v.to(dev) for k, v in t.items()}
+        fn = lambda: fused_attn_hyb(g["q"], g["kp"], g["vp"], g["kn"], g["vn"], g["msk"])  # noqa: E731
+        for _ in range(warm):
+            fn()
+        us = _median_launch_us(torch, fn, reps, flush)
+        H, M, D = c["q"].shape
+        HK, NP, _ = c["kp"].shape
+        NN = c["kn"].shape[1]
+        algo = 4 * (2 * HK * (NP + NN) * D + 2 * H * M * D) + M * NN
+        # eager SDPA on the CPU (dispatch's original path): fp32, additive mask over [prefix | nodes]
+        G = H // HK
+        qc = t["q"][None]
+        kc = torch.cat([t["kp"], t["kn"]], 1).repeat_interleave(G, 0)[None]
+        vc = torch.cat([t["vp"], t["vn"]], 1).repeat_interleave(G, 0)[None]
+        mask = torch.zeros(M, NP + NN)
+        mask[:, NP:] = torch.where(t["msk"], 0.0, float("-inf"))
+        cpu = lambda: torch.nn.functional.scaled_dot_product_attention(qc, kc, vc, attn_mask=mask)  # noqa: E731
+        cpu()
+        cpu_ms = _median_cpu_ms(cpu, 20)
+        lines.append({"op": "fused_attn_hyb fp32 (config 1)", "shape": f"H{H}/{HK} M{M} NP{NP} NN{NN} D{D}",
+                      "us": us, "algorithmic_bytes": algo})
+        lines[-1]["cpu_ms"] = cpu_ms
+    else:
+        from respect_b200.kernels.rmsnorm import rmsnorm
+        from respect_b200.system.fused import rope, silu_mul
+        gen = torch.Generator().manual_seed(0)
+        x = torch.randn(128, 3584, generator=gen).to(torch.bfloat16)
+        w = (torch.rand(3584, generator=gen) + 0.5).to(torch.bfloat16)
+        rng = np.random.default_rng(0)
+        parents = [-1] + [int(rng.integers(0, i)) for i in range(1, 128)]
+        depth = [0] * 128
+        for i in range(1, 128):
+            depth[i] = depth[parents[i]] + 1
+        pos = torch.tensor([3000 + d for d in depth], dtype=torch.float32)
+        inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float32) / 128))
+        f = pos[:, None] * inv[None]
+        emb = torch.cat([f, f], -1)
+        cos, sin = emb.cos().to(torch.bfloat16)[None], emb.sin().to(torch.bfloat16)[None]
+        q = torch.randn(1, 28, 128, 128, generator=gen).to(torch.bfloat16)
+        k = torch.randn(1, 4, 128, 128, generator=gen).to(torch.bfloat16)
+        gt = torch.randn(128, 18944, generator=gen).to(torch.bfloat16)
+        ut = torch.randn(128, 18944, generator=gen).to(torch.bfloat16)
+        xd, wd, cd, sd, qd, kd, gd, ud = (v.to(dev) for v in (x, w, cos, sin, q, k, gt, ut))
+
+        def rot(v):
+            return torch.cat([-v[..., 64:], v[..., :64]], -1)
+
+        def hf_norm(v, wt):
+            vf = v.float()
+            return wt * (vf * torch.rsqrt(vf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(v.dtype)
+        ops = [("rmsnorm (row-invariant) [128, 3584]", lambda: rmsnorm(xd, wd, 1e-6), lambda: hf_norm(x, w),
+                3 * 128 * 3584 * 2 + 3584 * 2),
+               ("rope q [1,28,128,128] + k [1,4,128,128]", lambda: (rope(qd, cd, sd), rope(kd, cd, sd)),
+                lambda: (q * cos[:, None] + rot(q) * sin[:, None], k * cos[:, None] + rot(k) * sin[:, None]),
+                2 * 2 * (28 + 4) * 128 * 128 + 2 * 2 * 128 * 128 * 2),
+               ("silu_mul [128, 18944]", lambda: silu_mul(gd, ud),
+                lambda: torch.nn.functional.silu(gt) * ut, 3 * 128 * 18944 * 2)]
+        for name, gpu_fn, cpu_fn, algo in ops:
+            for _ in range(warm):
+                gpu_fn()
+            us = _median_launch_us(torch, gpu_fn, reps, flush)
+            cpu_fn()
+            lines.append({"op": name, "us": us, "algorithmic_bytes": algo, "cpu_ms": _median_cpu_ms(cpu_fn, 20)})
+    for ln in lines:
+        ln.update({"kernel_case": args.kernel_case, "GBps": ln["algorithmic_bytes"] / (ln["us"] * 1e-6) / 1e9,
+                   "peak_hbm_gbs": hbm, "peak_source": src, "cpu_threads": threads,
+                   "cpu_over_gpu": ln["cpu_ms"] * 1e3 / ln["us"], "l2": "flushed before every timed launch",
+                   "launches": reps})
+        ln["frac"] = ln["GBps"] / hbm
+        print(json.dumps(ln), flush=True)
+
+
 def run_kernel_case(args):
     import torch
     from respect_b200.decoding.engine import DecoderConfig
@@ -529,7 +655,9 @@ def run_kernel_case(args):
 
 def main():
     args = parse()
-    if args.kernel_case:
+    if args.kernel_case in ("config1", "config2"):
+        run_config_case(args)
+    elif args.kernel_case:
         run_kernel_case(args)
     elif args.impl == "reference":
         run_reference(args)

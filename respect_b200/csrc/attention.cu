@@ -392,22 +392,14 @@ static int launch_nodes_r(const AttnDev& p, const float* part, int grid, cudaStr
 // of dependent loads, a block barrier per batch and a serial fold), so under
 // PDL more items per block made the pre-wait part outlast the prefix kernel
 // (measured on the config-3 step: 9.7 us after the prefix with one item,
-// 17.8 with two, 17.3 with three). The template keeps R for other shapes.
+// 17.8 with two, 17.3 with three), so only R = 1 is built.
 template <typename T>
 static int launch_nodes(const AttnDev& p, const float* part, cudaStream_t stream, bool pdl) {
   const int G = p.H / p.HK;
   if (G > kMaxGroup) return RB_ERR_UNSUPPORTED;
   const int items = p.M * p.HK;
   if (items <= 0) return RB_OK;
-  (void)pdl;
-  const int R = 1;
-  const int grid = (items + R - 1) / R;
-  switch (R) {
-    case 1: return launch_nodes_r<T, 1>(p, part, grid, stream, pdl);
-    case 2: return launch_nodes_r<T, 2>(p, part, grid, stream, pdl);
-    case 3: return launch_nodes_r<T, 3>(p, part, grid, stream, pdl);
-    default: return launch_nodes_r<T, 4>(p, part, grid, stream, pdl);
-  }
+  return launch_nodes_r<T, 1>(p, part, items, stream, pdl);
 }
 
 // ----------------------------------------------------------------- host
