@@ -477,28 +477,39 @@ def run_frame_replay(args):
 
 
 # ------------------------------------------------------------------ single-kernel cases
-def _median_launch_us(torch, fn, reps, flush):
-    """Median device time of fn() over `reps` launches, each preceded by an L2 flush
-    (a write of a buffer larger than L2) and bracketed by CUDA events. fn is captured
-    in a CUDA graph first, so the host's wrapper work stays out of the timed region."""
+def _median_launch_us(torch, fn, reps, flush, inner=20):
+    """Device time of one fn() launch that follows an L2 flush (a write of a buffer
+    larger than L2), net of the flush: two CUDA graphs, `inner` x (flush, fn) and
+    `inner` x (flush), each replayed between CUDA events; the median over `reps`
+    replays of their difference, divided by `inner`. One graph launch per `inner`
+    operations keeps the host and the launch latency out of the figure."""
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
         fn()
     torch.cuda.current_stream().wait_stream(side)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        fn()
-    ts = []
-    for _ in range(reps):
-        flush.zero_()
+    g_op, g_fl = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_op):
+        for _ in range(inner):
+            flush.zero_()
+            fn()
+    with torch.cuda.graph(g_fl):
+        for _ in range(inner):
+            flush.zero_()
+
+    def timed(g):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        graph.replay()
+        g.replay()
         e1.record()
         torch.cuda.synchronize()
-        ts.append(e0.elapsed_time(e1) * 1e3)
-    return statistics.median(ts)
+        return e0.elapsed_time(e1) * 1e3
+
+    g_op.replay()
+    g_fl.replay()
+    torch.cuda.synchronize()
+    diffs = [(timed(g_op) - timed(g_fl)) / inner for _ in range(max(reps // inner, 5))]
+    return statistics.median(diffs)
 
 
 def _median_cpu_ms(fn, reps):
@@ -592,7 +603,8 @@ def run_config_case(args):
     for ln in lines:
         ln.update({"kernel_case": args.kernel_case, "GBps": ln["algorithmic_bytes"] / (ln["us"] * 1e-6) / 1e9,
                    "peak_hbm_gbs": hbm, "peak_source": src, "cpu_threads": threads,
-                   "cpu_over_gpu": ln["cpu_ms"] * 1e3 / ln["us"], "l2": "flushed before every timed launch",
+                   "cpu_over_gpu": ln["cpu_ms"] * 1e3 / ln["us"],
+                   "l2": "flushed before every launch; the flush's own time subtracted",
                    "launches": reps})
         ln["frac"] = ln["GBps"] / hbm
         print(json.dumps(ln), flush=True)

@@ -90,9 +90,14 @@ __global__ void __launch_bounds__(128) attn_prefix_simt(const AttnDev p, float* 
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int r = warp * 4 + i;
-      float s = 0.f;
+      // four partial sums over d = 4k + e (fixed order), added pairwise at the end
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 8
-      for (int d = 0; d < D; ++d) s = fmaf(qs[r][d], ks[lane][d], s);
+      for (int d = 0; d < D; d += 4) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s4[e] = fmaf(qs[r][d + e], ks[lane][d + e], s4[e]);
+      }
+      float s = (s4[0] + s4[1]) + (s4[2] + s4[3]);
       s = kvalid ? s * scale2 : -INFINITY;
       const float tmax = warp_max(s);
       const float m_new = fmaxf(m[i], tmax);
@@ -142,7 +147,8 @@ __device__ __forceinline__ bool node_allowed(const AttnDev& p, int row, int j) {
 
 // Node phase. A row's allowed node slots are visited in slot order, in
 // batches of up to 32. Lane u scores the batch's u-th slot (q.k over the 128
-// dims in ascending order, fp32, times scale*log2(e)), then the batch is folded
+// dims in a fixed order: ascending for bf16 data, four interleaved partial sums
+// for fp32; times scale*log2(e)), then the batch is folded
 // one slot at a time, starting from an empty state:
 //   m' = max(m, s); a = 2^(m - m'); p = 2^(s - m'); acc = p*v + acc*a; l = l*a + p
 // (lane u of the fold owns dims [4u, 4u+4)). Every slot goes through exactly
@@ -192,17 +198,18 @@ __device__ __forceinline__ float dot128_smem<uint16_t>(const uint8_t* krow, cons
 }
 template <>
 __device__ __forceinline__ float dot128_smem<float>(const uint8_t* krow, const float* qs) {
-  float s = 0.f;
+  // four partial sums over d = 4c + e (fixed order), added pairwise at the end
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
   for (int c = 0; c < 32; ++c) {
     const float4 k4 = reinterpret_cast<const float4*>(krow)[c];
     const float4 q4 = reinterpret_cast<const float4*>(qs)[c];
-    s = fmaf(q4.x, k4.x, s);
-    s = fmaf(q4.y, k4.y, s);
-    s = fmaf(q4.z, k4.z, s);
-    s = fmaf(q4.w, k4.w, s);
+    s0 = fmaf(q4.x, k4.x, s0);
+    s1 = fmaf(q4.y, k4.y, s1);
+    s2 = fmaf(q4.z, k4.z, s2);
+    s3 = fmaf(q4.w, k4.w, s3);
   }
-  return s;
+  return (s0 + s1) + (s2 + s3);
 }
 
 // Running softmax state of one (row, head), lane-owned dims [4*lane, 4*lane+4).
