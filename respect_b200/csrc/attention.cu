@@ -43,7 +43,7 @@ template <> __device__ __forceinline__ void ld4<uint16_t>(const uint16_t* p, flo
 template <typename T>
 __global__ void __launch_bounds__(128) attn_prefix_simt(const AttnDev p, float* __restrict__ part, int nchunks) {
   constexpr int D = 128, TK = 32, RB = 16;
-  __shared__ float ks[TK][D + 1];
+  __shared__ __align__(16) float ks[TK][D + 4];  // 16-byte rows; a quarter-warp's float4 reads hit distinct banks
   __shared__ __align__(16) float vs[TK][D];
   __shared__ __align__(16) float qs[RB][D];
   const int c = blockIdx.x, h = blockIdx.y, r0 = blockIdx.z * RB;
@@ -87,39 +87,62 @@ __global__ void __launch_bounds__(128) attn_prefix_simt(const AttnDev p, float* 
     }
     __syncthreads();
     const bool kvalid = kt + lane < k1;
+    // Scores of the warp's four rows for key `lane`, in one pass over the dims:
+    // each float4 of the key row feeds the four rows (q rows are broadcast reads).
+    // Per row: four partial sums over d = 4k + e (fixed order), added pairwise.
+    float s4[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s4[i][e] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < D; d += 4) {
+      const float4 k4 = *reinterpret_cast<const float4*>(&ks[lane][d]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 q4 = *reinterpret_cast<const float4*>(&qs[warp * 4 + i][d]);
+        s4[i][0] = fmaf(q4.x, k4.x, s4[i][0]);
+        s4[i][1] = fmaf(q4.y, k4.y, s4[i][1]);
+        s4[i][2] = fmaf(q4.z, k4.z, s4[i][2]);
+        s4[i][3] = fmaf(q4.w, k4.w, s4[i][3]);
+      }
+    }
+    float pv[4], alpha[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int r = warp * 4 + i;
-      // four partial sums over d = 4k + e (fixed order), added pairwise at the end
-      float s4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-      for (int d = 0; d < D; d += 4) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) s4[e] = fmaf(qs[r][d + e], ks[lane][d + e], s4[e]);
-      }
-      float s = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      float s = (s4[i][0] + s4[i][1]) + (s4[i][2] + s4[i][3]);
       s = kvalid ? s * scale2 : -INFINITY;
       const float tmax = warp_max(s);
       const float m_new = fmaxf(m[i], tmax);
-      const float alpha = fast_exp2(m[i] - m_new);
+      alpha[i] = fast_exp2(m[i] - m_new);
       const float pj = fast_exp2(s - m_new);
       float psum = warp_sum(pj);
       psum = __shfl_sync(0xffffffffu, psum, 0);
       // bf16 inputs: the probabilities enter the value product as bf16 (attention.py:48).
-      const float pv = sizeof(T) == 2 ? round_bf16(pj) : pj;
-      float t[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-      for (int j = 0; j < TK; ++j) {
-        const float pb = __shfl_sync(0xffffffffu, pv, j);
-        const float4 v4 = *reinterpret_cast<const float4*>(&vs[j][lane * 4]);
-        t[0] = fmaf(pb, v4.x, t[0]); t[1] = fmaf(pb, v4.y, t[1]);
-        t[2] = fmaf(pb, v4.z, t[2]); t[3] = fmaf(pb, v4.w, t[3]);
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[i][e] = fmaf(acc[i][e], alpha, t[e]);
-      l[i] = fmaf(l[i], alpha, psum);
+      pv[i] = sizeof(T) == 2 ? round_bf16(pj) : pj;
+      l[i] = fmaf(l[i], alpha[i], psum);
       m[i] = m_new;
     }
+    // P V of the four rows; each value row (this lane's four dims) is read once.
+    float t[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) t[i][e] = 0.f;
+#pragma unroll 4
+    for (int j = 0; j < TK; ++j) {
+      const float4 v4 = *reinterpret_cast<const float4*>(&vs[j][lane * 4]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float pb = __shfl_sync(0xffffffffu, pv[i], j);
+        t[i][0] = fmaf(pb, v4.x, t[i][0]); t[i][1] = fmaf(pb, v4.y, t[i][1]);
+        t[i][2] = fmaf(pb, v4.z, t[i][2]); t[i][3] = fmaf(pb, v4.w, t[i][3]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[i][e] = fmaf(acc[i][e], alpha[i], t[i][e]);
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
