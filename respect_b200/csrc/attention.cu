@@ -38,14 +38,27 @@ template <> __device__ __forceinline__ void ld4<uint16_t>(const uint16_t* p, flo
 }
 
 // ----------------------------------------------------------------- prefix (SIMT)
-// Block = 4 warps = 16 query rows of one head over one prefix chunk. Key tiles
-// of 32 staged in shared memory; lane j scores key j of the tile.
+// fp32 data. Block = 4 warps = 16 query rows of one head over one prefix
+// chunk. Key tiles of 32 keys are copied into shared memory with cp.async, two
+// buffers deep (tile t+1 lands while tile t is computed); lane j scores key j
+// of the tile.
+constexpr int kSimtTK = 32, kSimtRB = 16, kSimtKPitch = 128 + 4;  // K rows: 16-byte aligned, float4 reads conflict-free
+constexpr int kSimtSmem = (2 * kSimtTK * kSimtKPitch + 2 * kSimtTK * 128 + kSimtRB * 128) * 4;
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
+  // src_bytes = 0 copies nothing and zero-fills the 16 bytes
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+
 template <typename T>
 __global__ void __launch_bounds__(128) attn_prefix_simt(const AttnDev p, float* __restrict__ part, int nchunks) {
-  constexpr int D = 128, TK = 32, RB = 16;
-  __shared__ __align__(16) float ks[TK][D + 4];  // 16-byte rows; a quarter-warp's float4 reads hit distinct banks
-  __shared__ __align__(16) float vs[TK][D];
-  __shared__ __align__(16) float qs[RB][D];
+  static_assert(sizeof(T) == 4, "the CUDA-core prefix serves fp32 data (bf16 runs on the tensor cores)");
+  constexpr int D = 128, TK = kSimtTK, RB = kSimtRB;
+  extern __shared__ __align__(16) float simt_smem[];
+  auto ks = reinterpret_cast<float(*)[TK][kSimtKPitch]>(simt_smem);              // [2][TK][pitch]
+  auto vs = reinterpret_cast<float(*)[TK][D]>(simt_smem + 2 * TK * kSimtKPitch);  // [2][TK][D]
+  auto qs = reinterpret_cast<float(*)[D]>(simt_smem + 2 * TK * kSimtKPitch + 2 * TK * D);
   const int c = blockIdx.x, h = blockIdx.y, r0 = blockIdx.z * RB;
   const int kvh = h / (p.H / p.HK);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -60,6 +73,18 @@ __global__ void __launch_bounds__(128) attn_prefix_simt(const AttnDev p, float* 
   const T* q = static_cast<const T*>(p.q);
   const T* kp = static_cast<const T*>(p.kp);
   const T* vp = static_cast<const T*>(p.vp);
+  // Tile starting at key kt into buffer b; keys past the chunk end are zero-filled.
+  auto stage = [&](int b, int kt) {
+    for (int i = threadIdx.x; i < TK * D / 4; i += blockDim.x) {
+      const int j = i / (D / 4), d4 = (i % (D / 4)) * 4;
+      const bool ok = kt + j < k1;
+      const int key = ok ? kt + j : k0;
+      cp_async16(&ks[b][j][d4], kp + kvh * p.skph + static_cast<int64_t>(key) * p.skpn + d4, ok ? 16u : 0u);
+      cp_async16(&vs[b][j][d4], vp + kvh * p.svph + static_cast<int64_t>(key) * p.svpn + d4, ok ? 16u : 0u);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  stage(0, k0);
 
   for (int i = threadIdx.x; i < RB * D; i += blockDim.x) {
     const int r = i / D, d = i % D;
@@ -73,19 +98,15 @@ __global__ void __launch_bounds__(128) attn_prefix_simt(const AttnDev p, float* 
     for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
   }
   const float scale2 = p.sm_scale * kLog2e;
-  for (int kt = k0; kt < k1; kt += TK) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < TK * D / 4; i += blockDim.x) {
-      const int j = i / (D / 4), d4 = (i % (D / 4)) * 4;
-      float kv[4] = {0.f, 0.f, 0.f, 0.f}, vv[4] = {0.f, 0.f, 0.f, 0.f};
-      if (kt + j < k1) {
-        ld4(kp + kvh * p.skph + static_cast<int64_t>(kt + j) * p.skpn + d4, kv);
-        ld4(vp + kvh * p.svph + static_cast<int64_t>(kt + j) * p.svpn + d4, vv);
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) { ks[j][d4 + e] = kv[e]; vs[j][d4 + e] = vv[e]; }
+  for (int kt = k0, tile = 0; kt < k1; kt += TK, ++tile) {
+    const int b = tile & 1;
+    if (kt + TK < k1) {
+      stage(b ^ 1, kt + TK);  // its buffer was last read by the previous tile, which every warp has finished
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
-    __syncthreads();
+    __syncthreads();  // this tile (and q) visible to every warp
     const bool kvalid = kt + lane < k1;
     // Scores of the warp's four rows for key `lane`, in one pass over the dims:
     // each float4 of the key row feeds the four rows (q rows are broadcast reads).
@@ -97,7 +118,7 @@ __global__ void __launch_bounds__(128) attn_prefix_simt(const AttnDev p, float* 
       for (int e = 0; e < 4; ++e) s4[i][e] = 0.f;
 #pragma unroll 4
     for (int d = 0; d < D; d += 4) {
-      const float4 k4 = *reinterpret_cast<const float4*>(&ks[lane][d]);
+      const float4 k4 = *reinterpret_cast<const float4*>(&ks[b][lane][d]);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float4 q4 = *reinterpret_cast<const float4*>(&qs[warp * 4 + i][d]);
@@ -118,8 +139,7 @@ __global__ void __launch_bounds__(128) attn_prefix_simt(const AttnDev p, float* 
       const float pj = fast_exp2(s - m_new);
       float psum = warp_sum(pj);
       psum = __shfl_sync(0xffffffffu, psum, 0);
-      // bf16 inputs: the probabilities enter the value product as bf16 (attention.py:48).
-      pv[i] = sizeof(T) == 2 ? round_bf16(pj) : pj;
+      pv[i] = pj;
       l[i] = fmaf(l[i], alpha[i], psum);
       m[i] = m_new;
     }
@@ -131,7 +151,7 @@ __global__ void __launch_bounds__(128) attn_prefix_simt(const AttnDev p, float* 
       for (int e = 0; e < 4; ++e) t[i][e] = 0.f;
 #pragma unroll 4
     for (int j = 0; j < TK; ++j) {
-      const float4 v4 = *reinterpret_cast<const float4*>(&vs[j][lane * 4]);
+      const float4 v4 = *reinterpret_cast<const float4*>(&vs[b][j][lane * 4]);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float pb = __shfl_sync(0xffffffffu, pv[i], j);
@@ -143,6 +163,7 @@ __global__ void __launch_bounds__(128) attn_prefix_simt(const AttnDev p, float* 
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[i][e] = fmaf(acc[i][e], alpha[i], t[i][e]);
+    __syncthreads();  // every warp is done with buffer b before the tile after next is copied into it
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -491,7 +512,10 @@ int attn_launch(const rb_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t s
   if (nchunks > 0) {
     if (a->dtype == RB_F32) {  // fp32: CUDA-core FFMA (the 1e-5 parity bar rules out tf32 MMAs)
       dim3 grid(nchunks, a->H, (a->M + 15) / 16);
-      attn_prefix_simt<float><<<grid, 128, 0, stream>>>(p, part, nchunks);
+      if (cudaFuncSetAttribute(attn_prefix_simt<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSimtSmem) !=
+          cudaSuccess)
+        return RB_ERR_CUDA;
+      attn_prefix_simt<float><<<grid, 128, kSimtSmem, stream>>>(p, part, nchunks);
       if (cudaGetLastError() != cudaSuccess) return RB_ERR_CUDA;
     } else {  // bf16: tcgen05 QK^T / PV with TMA-staged tiles
       CUtensorMap tq, tk, tv;
