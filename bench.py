@@ -72,6 +72,8 @@ def parse():
     ap.add_argument("--kernel-case", default=None, choices=["gemm_gate_up", "attention", "config1", "config2"])
     ap.add_argument("--workload", default="verify_step", choices=["verify_step", "frame_replay"])
     ap.add_argument("--streams", type=int, default=16)
+    ap.add_argument("--one-cuda-stream", action="store_true",
+                    help="frame_replay: all frame streams' work on one CUDA stream")
     ap.add_argument("--nodes", type=int, default=NODES, help="verify_step: trie nodes (config 3: 128)")
     ap.add_argument("--prefix", type=int, default=PROMPT, help="verify_step: prompt tokens (config 3: 3000)")
     args = ap.parse_args()
@@ -404,7 +406,7 @@ def run_frame_replay(args):
 
     cfg = DecoderConfig.baseline_7b()
     w = DecoderWeights.random(cfg, dev, seed=0)
-    rcfg = ReplayConfig(streams=args.streams, seed=1000 + rank)
+    rcfg = ReplayConfig(streams=args.streams, seed=1000 + rank, shared_cuda_stream=args.one_cuda_stream)
     rep = FrameReplay(w, rcfg)
     warm = rep.run(args.warmup)
     if world > 1:
@@ -456,6 +458,7 @@ def run_frame_replay(args):
                                        "with the previous frame, 256-node tries (4 chains of 48 + continuation "
                                        "nodes), 80 committed tokens per frame",
                            "streams_per_gpu": rcfg.streams, "frames_per_stream": args.steps,
+                           "cuda_streams": 1 if rcfg.shared_cuda_stream else rcfg.streams,
                            "parallelism": f"replicas{world}",
                            "l2": "inputs larger than L2 (14.1 GB weights per step)"},
                 "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

@@ -81,7 +81,11 @@ RB_API int rb_device_error(int* code, int clear);
  * are accumulated one at a time in slot order and masked slots are skipped, so
  * a row's result depends only on its own allowed keys and their order. All
  * accumulation is fp32, the output is cast once.
- * Innermost strides (sqd, skpd, ...) must be 1. dtype RB_F32 or RB_BF16. */
+ * Innermost strides (sqd, skpd, ...) must be 1. dtype RB_F32 or RB_BF16.
+ * Layout limits (RB_ERR_UNSUPPORTED otherwise): D = 128; other strides in
+ * multiples of 4 elements and bases aligned to 4 elements; kp / vp (bf16) and
+ * kn / vn (both dtypes) in whole 16-byte rows: strides and bases multiples of
+ * 16 bytes. */
 typedef struct rb_attn_args {
   int dtype;
   int H, M, D, HK, NP, NN;

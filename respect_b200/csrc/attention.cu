@@ -487,6 +487,14 @@ int attn_validate(const rb_attn_args* a) {
                         nod ? a->vn : nullptr, a->out};
   for (const void* ptr : ptrs)
     if (ptr && (reinterpret_cast<uintptr_t>(ptr) % (4 * eb)) != 0) return RB_ERR_UNSUPPORTED;
+  // Node K / V rows are staged in shared memory with 16-byte copies: their bases
+  // and row / head strides must be whole 16-byte units (8 bf16 or 4 fp32 elements).
+  if (nod) {
+    const int64_t vec = 16 / eb;
+    if (a->sknn % vec || a->svnn % vec || a->sknh % vec || a->svnh % vec ||
+        (reinterpret_cast<uintptr_t>(a->kn) & 15) || (reinterpret_cast<uintptr_t>(a->vn) & 15))
+      return RB_ERR_UNSUPPORTED;
+  }
   return RB_OK;
 }
 

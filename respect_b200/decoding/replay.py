@@ -60,6 +60,7 @@ class ReplayConfig:
     eos: int = -1
     datastore_key_len: int = 2
     seed: int = 0
+    shared_cuda_stream: bool = False  # every frame stream's work on one CUDA stream, in host order
 
     def max_slots(self) -> int:
         # the last round writes its nodes after at most commit_tokens - 1 committed tokens
@@ -127,9 +128,9 @@ def round_trie(root: int, cands: list, cfg: ReplayConfig, vocab: int, rng: np.ra
 
 
 class _Stream:
-    def __init__(self, idx: int, eng: VerifyEngine, cfg: ReplayConfig):
+    def __init__(self, idx: int, eng: VerifyEngine, cfg: ReplayConfig, cuda=None):
         self.idx, self.eng, self.cfg = idx, eng, cfg
-        self.cuda = torch.cuda.Stream(eng.device)
+        self.cuda = cuda if cuda is not None else torch.cuda.Stream(eng.device)
         self.rng = np.random.default_rng([cfg.seed, idx])
         self.history = CocHistory(cfg.eos)
         self.store = Datastore.empty(cfg.datastore_key_len)
@@ -168,7 +169,8 @@ class FrameReplay:
         for i in range(cfg.streams):
             engines.append(VerifyEngine(weights, max_rows=rows, max_slots=cfg.max_slots(),
                                         share_weights=engines[0] if engines else None))
-        self.streams = [_Stream(i, e, cfg) for i, e in enumerate(engines)]
+        shared = torch.cuda.Stream(engines[0].device) if cfg.shared_cuda_stream else None
+        self.streams = [_Stream(i, e, cfg, shared) for i, e in enumerate(engines)]
         self.stats = ReplayStats()
         self.keep_records = False
 

@@ -46,11 +46,11 @@ def _check(w, rcfg, rep, stats):
         ref.close()
 
 
-@pytest.mark.parametrize("shared", [0.9, 1.0])
-def test_replay_streams_equal_sequential(model, shared):
+@pytest.mark.parametrize("shared,one_cuda_stream", [(0.9, False), (1.0, True)])
+def test_replay_streams_equal_sequential(model, shared, one_cuda_stream):
     cfg, w = model
     rcfg = ReplayConfig(streams=3, prompt_len=200, shared_frac=shared, trie_nodes=64, chains=4, chain_len=12,
-                        commit_tokens=20, prefill_chunk=64, seed=7)
+                        commit_tokens=20, prefill_chunk=64, seed=7, shared_cuda_stream=one_cuda_stream)
     rep = FrameReplay(w, rcfg)
     try:
         stats = rep.run(3, keep_records=True)

@@ -77,6 +77,30 @@ def test_capi_rejects_bad_arguments_without_a_gpu():
     assert lib.rb_engine_workspace_bytes(None) == 0
 
 
+def test_attention_rejects_node_rows_not_in_16_byte_units():
+    """Node K/V rows are copied in 16-byte pieces: a bf16 row stride of 132
+    elements (264 bytes) or a base off a 16-byte boundary is refused with
+    RB_ERR_UNSUPPORTED before any CUDA call (the pointers here are never read)."""
+    from respect_b200 import _lib
+    lib = _lib.lib()
+
+    def args(sknn=128, kn=0x100000, dtype=_lib.RB_BF16):
+        a = _lib.AttnArgs()
+        a.dtype, a.H, a.HK, a.D, a.M, a.NP, a.NN = dtype, 28, 4, 128, 16, 0, 32
+        a.q, a.sqh, a.sqm, a.sqd = 0x200000, 16 * 128, 128, 1
+        a.kn, a.sknh, a.sknn, a.sknd = kn, 32 * sknn, sknn, 1
+        a.vn, a.svnh, a.svnn, a.svnd = 0x300000, 32 * 128, 128, 1
+        a.msk, a.mask_kind, a.smm, a.smn = 0x400000, _lib.RB_MASK_BOOL, 32, 1
+        a.out, a.soh, a.som, a.sod = 0x500000, 16 * 128, 128, 1
+        a.sm_scale = 0.088
+        return a
+
+    for bad in (args(sknn=132), args(kn=0x100008), args(kn=0x100004)):
+        assert lib.rb_fused_attn_hyb(ctypes.byref(bad), None, 0, None) == 2
+    # the same call with 16-byte rows passes validation and only then asks for a workspace
+    assert lib.rb_fused_attn_hyb(ctypes.byref(args()), None, 0, None) == 6
+
+
 def test_engine_config_validation():
     from respect_b200.decoding import engine as E
     lib = __import__("respect_b200._lib", fromlist=["x"]).lib()
