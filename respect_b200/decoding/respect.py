@@ -68,6 +68,12 @@ class DecodeResult:
     verify_ms: float = 0.0
 
 
+def _sync(device) -> None:
+    """Wait for the device's queued work (timing fields); nothing to wait for off CUDA."""
+    if torch.device(device).type == "cuda":
+        torch.cuda.synchronize(device)
+
+
 def _fit(capacities, n: int) -> int:
     for c in sorted(capacities):
         if c >= n:
@@ -144,7 +150,7 @@ class RespectDecoder:
         datastore's drive index inside the timed region.
         """
         datastore = datastore if datastore is not None else Datastore.empty(self.cfg.datastore_key_len)
-        torch.cuda.synchronize(self.eng.device)
+        _sync(self.eng.device)
         t0 = time.perf_counter()
         insert_ms = 0.0
         if new_coc is not None:
@@ -164,7 +170,7 @@ class RespectDecoder:
         else:
             tokens = self._follow(fs, acc, rec, datastore, res)
             res.target_runs = 1 + res.follow_rounds
-        torch.cuda.synchronize(self.eng.device)
+        _sync(self.eng.device)
         t1 = time.perf_counter()
         res.tokens = [int(x) for x in tokens]
         res.initial_ms = (tm - t0) * 1000
