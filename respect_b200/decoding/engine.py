@@ -362,14 +362,7 @@ class VerifyEngine:
         toks = np.asarray(tokens, np.int32)
         if len(toks) > self.max_slots:
             raise ValueError(f"prompt of {len(toks)} tokens exceeds max_slots {self.max_slots}")
-        start = 0
-        if reuse is not None:
-            old = np.asarray(reuse, np.int32)
-            n = min(len(old), len(toks))
-            diff = np.flatnonzero(old[:n] != toks[:n])
-            lcp = int(diff[0]) if len(diff) else n
-            # the last chunk always runs: its last row's greedy pick is the first token
-            start = min((lcp // chunk) * chunk, ((len(toks) - 1) // chunk) * chunk)
+        start = prefill_start(toks, reuse, chunk)
         for s in range(start, len(toks), chunk):
             part = toks[s:s + chunk]
             n = len(part)
@@ -387,6 +380,23 @@ class VerifyEngine:
             self.close()
         except Exception:
             pass
+
+
+def prefill_start(tokens, reuse, chunk: int) -> int:
+    """First prompt position a chunked prefill recomputes when the buffer holds the KV of
+    `reuse` (prefilled with the same chunk): the start of the chunk holding the first
+    token that differs, but no later than the start of the last chunk (which always runs:
+    its last row's greedy pick is the token after the prompt). 0 without `reuse`."""
+    toks = np.asarray(tokens)
+    if reuse is None or len(toks) == 0:
+        return 0
+    if chunk <= 0:
+        raise ValueError(f"chunk must be positive, got {chunk}")
+    old = np.asarray(reuse)
+    n = min(len(old), len(toks))
+    diff = np.flatnonzero(old[:n] != toks[:n])
+    lcp = int(diff[0]) if len(diff) else n
+    return min((lcp // chunk) * chunk, ((len(toks) - 1) // chunk) * chunk)
 
 
 def _view(ptr: int, shape, dtype, device) -> torch.Tensor:

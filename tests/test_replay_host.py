@@ -50,3 +50,23 @@ def test_frame_prompts_share_the_configured_fraction():
     # one contiguous block of 10% (a random token may repeat the old one)
     assert len(changed) <= 410 and len(changed) > 380
     assert changed[-1] - changed[0] < 410
+
+
+def test_prefill_reuse_start():
+    from respect_b200.decoding.engine import prefill_start
+    p = np.arange(1000)
+    assert prefill_start(p, None, 256) == 0
+    assert prefill_start(p, p, 256) == 768                # same prompt: only the last chunk
+    q = p.copy(); q[0] = -1
+    assert prefill_start(q, p, 256) == 0                  # first token changed
+    q = p.copy(); q[300] = -1
+    assert prefill_start(q, p, 256) == 256                # the chunk holding token 300 on
+    q = p.copy(); q[255] = -1
+    assert prefill_start(q, p, 256) == 0
+    q = p.copy(); q[256] = -1
+    assert prefill_start(q, p, 256) == 256
+    assert prefill_start(p[:512], p, 256) == 256          # old prompt longer: last chunk of the new
+    assert prefill_start(p, p[:600], 256) == 512          # old prompt shorter: from its last whole chunk
+    assert prefill_start(p[:256], p, 256) == 0            # one chunk: it always runs
+    assert prefill_start(p[:0], p, 256) == 0              # empty prompt: nothing to run
+    assert prefill_start(p[:513], p[:513], 256) == 512
