@@ -159,16 +159,27 @@ class _Stream:
 class FrameReplay:
     """`streams` frame streams on one device, one engine each, weights shared."""
 
-    def __init__(self, weights: DecoderWeights, cfg: ReplayConfig = ReplayConfig(), graph: bool = True):
+    def __init__(self, weights: DecoderWeights, cfg: ReplayConfig = ReplayConfig(), graph: bool = True,
+                 engines: list | None = None):
+        """`engines`: one engine per stream, built by the caller (with at least
+        max(trie_nodes, prefill_chunk) rows and cfg.max_slots() slots); by default one
+        VerifyEngine per stream on shared packed weights."""
         self.cfg = cfg
         self.w = weights
         self.graph = graph
         self.vocab = weights.cfg.vocab
         rows = max(cfg.trie_nodes, cfg.prefill_chunk)
-        engines: list = []
-        for i in range(cfg.streams):
-            engines.append(VerifyEngine(weights, max_rows=rows, max_slots=cfg.max_slots(),
-                                        share_weights=engines[0] if engines else None))
+        if engines is None:
+            engines = []
+            for i in range(cfg.streams):
+                engines.append(VerifyEngine(weights, max_rows=rows, max_slots=cfg.max_slots(),
+                                            share_weights=engines[0] if engines else None))
+        elif len(engines) != cfg.streams:
+            raise ValueError(f"{len(engines)} engines for {cfg.streams} streams")
+        for e in engines:
+            if e.max_rows < rows or e.max_slots < cfg.max_slots():
+                raise ValueError(f"engine of {e.max_rows} rows / {e.max_slots} slots is too small for "
+                                 f"{rows} rows / {cfg.max_slots()} slots")
         shared = torch.cuda.Stream(engines[0].device) if cfg.shared_cuda_stream else None
         self.streams = [_Stream(i, e, cfg, shared) for i, e in enumerate(engines)]
         self.stats = ReplayStats()
