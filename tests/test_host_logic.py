@@ -113,3 +113,34 @@ def test_engine_config_validation():
     cfg = E.DecoderConfig.baseline_7b()
     # weights streamed per step: 6.525 G layer params + 0.545 G lm_head (bf16)
     assert abs(cfg.weight_bytes_per_step() / 1e9 - 14.14) < 0.01
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    """Without the native library, loading it raises and so does every operator
+    (CPU tensors are refused before that); nothing falls back to a CPU or library
+    implementation."""
+    import subprocess
+    import sys
+    code = (
+        "import torch, respect_b200\n"
+        "from respect_b200.kernels.rmsnorm import rmsnorm\n"
+        "from respect_b200.system.fused import silu_mul\n"
+        "try:\n"
+        "    respect_b200.load()\n"
+        "except ImportError as e:\n"
+        "    assert 'no fallback' in str(e), e\n"
+        "else:\n"
+        "    raise SystemExit('loaded a library that is not there')\n"
+        "for f, a in ((rmsnorm, (torch.ones(2, 8, dtype=torch.bfloat16), torch.ones(8, dtype=torch.bfloat16), 1e-6)),\n"
+        "             (silu_mul, (torch.ones(4, dtype=torch.bfloat16), torch.ones(4, dtype=torch.bfloat16)))):\n"
+        "    try:\n"
+        "        f(*a)\n"
+        "    except (ImportError, ValueError) as e:\n"
+        "        assert 'no fallback' in str(e) or 'no CPU path' in str(e), e\n"
+        "    else:\n"
+        "        raise SystemExit('computed without the library')\n"
+        "print('raised')\n")
+    env = dict(__import__("os").environ, RESPECT_B200_LIB=str(tmp_path / "absent.so"))
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300,
+                       cwd=str(__import__("pathlib").Path(__file__).resolve().parent.parent))
+    assert r.returncode == 0 and "raised" in r.stdout, r.stdout + r.stderr
