@@ -46,6 +46,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -196,7 +197,7 @@ class Clocks:
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+        self.path = Path(tempfile.gettempdir()) / f"respect_b200_clocks_{os.getpid()}.csv"
 
     def __enter__(self):
         try:

@@ -13,7 +13,7 @@ tiny_model(0) re-creates them (seeded HF init on CPU), and the fixture keeps a
 per-tensor checksum that the tests assert before using them.
 
 Two shims adapt the reference (written for transformers 4.57) to the image's
-transformers 5.5, as in the survey's probe: Cache.update no longer passes
+transformers 5.5: Cache.update no longer passes
 cache_kwargs["cache_position"] (the window layer takes the positions from the
 harness), and on CPU in fp32 eager SDPA needs the bf16 verify mask cast to the
 query dtype.
