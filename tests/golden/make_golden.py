@@ -20,6 +20,9 @@ What runs (all on CPU, in the build container where the reference is importable)
   * a 2-layer random-init Qwen3-VL text model verified through
     respect.decoding.verify.verify_trie with and without
     respect.kernels.patch.dedicated_kernels, fp32                       -> model.npz
+  * two verification rounds (verify_trie, greedy_token, walk, compact) of
+    the reference's eager path on a 4-layer random Qwen3-VL text model, and
+    its token-by-token decoding, fp32, for 3 prompts (``--only token``) -> token.npz
 
 Inputs come from oracle.inputs (seeded numpy); fixtures store outputs plus a
 checksum of the inputs, so the tests regenerate the inputs and compare.
@@ -278,6 +281,10 @@ def main():
         sys.path.insert(0, str(HERE))
         import make_model_golden
         make_model_golden.generate(HERE)
+    if "token" in only:
+        sys.path.insert(0, str(HERE))
+        import make_token_golden
+        make_token_golden.generate(HERE)
     print("fixtures written to", HERE)
 
 

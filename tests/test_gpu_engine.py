@@ -175,6 +175,44 @@ def test_engine_equals_operator_composition_7b_layer():
         eng.close()
 
 
+def test_engine_layout_sweep(tiny):
+    """The reference's layout sweep (scripts/run_kernel_order.py:32-125) through the
+    engine's trie path: a 26-token chain whose nodes sit consecutively, at
+    0-17 + 200-207, or at 5 seeded random sorted slots of a 256-row step (the other
+    rows are seeded single-token roots) gives the chain's logits and K / V bitwise
+    equal in every layout."""
+    import random
+    cfg, w, small = tiny
+    eng = VerifyEngine(w, max_rows=256, max_slots=1024, share_weights=small)
+    rng = np.random.default_rng(6)
+    P, N, NPAD = 300, 26, 256
+    eng.prefill(rng.integers(0, cfg.vocab, P), chunk=128)
+    chain = [int(t) for t in rng.integers(0, cfg.vocab, N)]
+    r = random.Random(0)
+    layouts = [list(range(N)), list(range(18)) + list(range(200, 200 + N - 18))]
+    layouts += [sorted(r.sample(range(NPAD), N)) for _ in range(5)]
+    ref = None
+    for slots in layouts:
+        ids = rng.integers(0, cfg.vocab, NPAD).astype(np.int32)
+        parents = np.full(NPAD, -1, np.int32)
+        depths = np.zeros(NPAD, np.int32)
+        for i, s in enumerate(slots):
+            ids[s] = chain[i]
+            parents[s] = slots[i - 1] if i else -1
+            depths[s] = i
+        eng.step(ids, parents, depths, 3, P)
+        sl = torch.tensor(slots, device=DEV)
+        got = (eng.logits(NPAD)[sl].clone(), [k[:, P + 3 + sl].clone() for k in eng.kc],
+               [v[:, P + 3 + sl].clone() for v in eng.vc])
+        if ref is None:
+            ref = got
+            continue
+        assert torch.equal(got[0], ref[0]), slots
+        for a, b in zip(got[1] + got[2], ref[1] + ref[2]):
+            assert torch.equal(a, b), slots
+    eng.close()
+
+
 def test_device_accept_matches_host_walk(tiny):
     """rb_engine_accept (walk + compaction on the device) equals the host walk
     (acceptance.py:26-46) followed by rb_engine_compact: the same path, tokens and
@@ -301,8 +339,8 @@ def _path_rows(tree, path_toks):
 def test_7b_invariance_sweep(big):
     """Config 4: a fixed 32-token path, inside tries of 1 / 8 / 64 / 256 / 512 nodes
     (the path's first n tokens where n < 32; seeded siblings top up the rest), at
-    every prefix length of SWEEP_P: the committed-node logits and K / V equal the
-    same tokens decoded one at a time (1-node steps), bitwise.
+    every prefix length of SWEEP_P: the committed-node logits and the K / V of all
+    28 layers equal the same tokens decoded one at a time (1-node steps), bitwise.
 
     One prefill of 3,129 tokens serves every prefix length: a token's KV depends
     only on the tokens before it, and the lengths run from the longest down, so a
@@ -317,8 +355,8 @@ def test_7b_invariance_sweep(big):
         for i, t in enumerate(path_toks):
             eng.step(np.array([t], np.int32), np.array([-1], np.int32), np.array([0], np.int32), i, P)
             ar_rows.append(eng.logits(1)[0].clone())
-        ar_k = [k[:, P:P + 32].clone() for k in eng.kc[:2]]
-        ar_v = [v[:, P:P + 32].clone() for v in eng.vc[:2]]
+        ar_k = [k[:, P:P + 32].clone() for k in eng.kc]
+        ar_v = [v[:, P:P + 32].clone() for v in eng.vc]
         for n in (1, 8, 64, 256, 512):
             L = min(n, 32)
             tree = trie_with_path(np.random.default_rng(n + P), path_toks[:L], n, cfg.vocab)
@@ -331,6 +369,6 @@ def test_7b_invariance_sweep(big):
             for d, node in enumerate(idx):
                 assert torch.equal(lg[node], ar_rows[d]), (P, n, d)
             sl = P + torch.tensor(idx, device=DEV)
-            for li in range(2):
+            for li in range(cfg.n_layers):
                 assert torch.equal(eng.kc[li][:, sl], ar_k[li][:, :L]), (P, n, li)
                 assert torch.equal(eng.vc[li][:, sl], ar_v[li][:, :L]), (P, n, li)

@@ -92,6 +92,50 @@ def test_attention_slot_layout_invariance(dtype):
     assert torch.equal(outs[0], outs[1])
 
 
+# The reference's layout sweep (scripts/run_kernel_order.py:32-125): the same 26
+# node keys / values placed consecutively, at 0-17 + 200-207, and at 5 seeded
+# random sorted slot sets inside NPAD = 256 node slots; one query row attends
+# them (padding rows open slot 0).
+LAYOUT_NPAD, LAYOUT_N = 256, 26
+
+
+def _layouts():
+    import random
+    r = random.Random(0)
+    out = [list(range(LAYOUT_N)), list(range(18)) + list(range(200, 200 + LAYOUT_N - 18))]
+    out += [sorted(r.sample(range(LAYOUT_NPAD), LAYOUT_N)) for _ in range(5)]
+    return out
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_attention_layout_sweep(dtype):
+    """Consecutive, scattered and 5 random layouts at NPAD=256 give bitwise equal
+    outputs (28 / 4 heads, a 3,000-key prefix, as in the config-3 step)."""
+    from respect_b200.kernels.attention import fused_attn_hyb
+    g = torch.Generator(device=DEV).manual_seed(11)
+    H, HK, D, NP = 28, 4, 128, 3000
+    q1 = (torch.randn(H, 1, D, device=DEV, generator=g) / D ** 0.5).to(dtype)
+    kp = torch.randn(HK, NP, D, device=DEV, generator=g).to(dtype)
+    vp = torch.randn(HK, NP, D, device=DEV, generator=g).to(dtype)
+    K = torch.randn(HK, LAYOUT_N, D, device=DEV, generator=g).to(dtype)
+    V = torch.randn(HK, LAYOUT_N, D, device=DEV, generator=g).to(dtype)
+    outs = []
+    for slots in _layouts():
+        kn = torch.zeros(HK, LAYOUT_NPAD, D, device=DEV, dtype=dtype)
+        vn = torch.zeros_like(kn)
+        msk = torch.zeros(64, LAYOUT_NPAD, device=DEV, dtype=torch.bool)
+        for i, c in enumerate(slots):
+            kn[:, c] = K[:, i]
+            vn[:, c] = V[:, i]
+            msk[0, c] = True
+        msk[1:, 0] = True
+        q = torch.zeros(H, 64, D, device=DEV, dtype=dtype)
+        q[:, 0] = q1[:, 0]
+        outs.append(fused_attn_hyb(q, kp, vp, kn, vn, msk)[:, 0].clone())
+    for o in outs[1:]:
+        assert torch.equal(outs[0], o)
+
+
 def test_attention_row_count_and_mask_kind_invariance():
     from respect_b200.kernels.attention import attn_call
     from respect_b200 import _lib
