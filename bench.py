@@ -17,8 +17,9 @@ N > 1: one process per GPU (torchrun), independent replicas (frame streams)
 with no collective on the data path; the timed region is bracketed by a
 barrier and the max over ranks is reported.
 
---impl reference: the reference's CPU path (the numpy oracle restating it,
-oracle/) on the host cores, on a bounded sample of the same step.
+--impl reference: the reference's CPU path on the host cores: whole verify
+steps of its eager bf16 forward at the config-3 model size (a torch restatement,
+oracle/torch_model.py), at most 20 timed steps.
 
 --workload frame_replay [--streams S]: the multi-stream frame replay (S frame
 streams per GPU, 4,096-token prompts, 256-node tries, 80 committed tokens per
@@ -131,58 +132,60 @@ def job_value(world: int, units_per_step: float, steps: int, ms: float) -> float
     return world * units_per_step * steps / (ms / 1e3)
 
 
-# ------------------------------------------------------------------ CPU sample (oracle)
-def cpu_sample(steps, warmup, seed=0, nodes=NODES, prompt=PROMPT, chain=CHAIN):
-    """One decoder layer of the step (`nodes` rows vs the `prompt`-token prefix; config 3:
-    128 vs 3000) plus 1/28 of the lm_head rows, in the numpy oracle; a step is 28 such samples."""
-    from oracle import model as omodel
-    from oracle.bf16 import round_bf16
+# ------------------------------------------------------------------ CPU baseline (whole steps)
+def cpu_steps(steps, warmup, nodes=NODES, prompt=PROMPT, chain=CHAIN, seed=0):
+    """Whole verify steps of the reference's eager path on the host cores: the full
+    28-layer config-3 model (hidden 3584, 28 / 4 heads of 128, FFN 18944, vocab
+    152,064) in bf16 through torch's CPU ops (oracle/torch_model.py, mode "eager":
+    HF's RMSNorm, linears, RoPE, SDPA with the additive trie mask and SiLU*mul, as
+    respect/decoding/verify.py:12-46 runs without the dedicated kernels), `nodes`
+    trie rows over a `prompt`-token prefix. Each timed step is one complete
+    forward; the metric counts the `chain` tokens the GPU step commits."""
+    import torch
+
+    from oracle import torch_model as tm
     from oracle.inputs import chain_seqs, top_up
     from respect_b200.candidates.trie import build_trie
+    h, L, H, HK, D, F, V = 3584, 28, 28, 4, 128, 18944, 152064
+    # all host threads (torchrun sets OMP_NUM_THREADS=1 for its workers)
+    torch.set_num_threads(os.cpu_count() or 1)
+    W = tm.random_weights_cpu(h, L, H, HK, D, F, V, seed=seed)
+    g = torch.Generator().manual_seed(seed + 1)
+    kc = [torch.randn(HK, prompt + nodes, D, generator=g).to(torch.bfloat16) for _ in range(L)]
+    vc = [torch.randn(HK, prompt + nodes, D, generator=g).to(torch.bfloat16) for _ in range(L)]
     rng = np.random.default_rng(seed)
-    h, H, HK, D, F, V = 3584, 28, 4, 128, 18944, 152064
-
-    def nrm(*s):
-        return round_bf16(rng.standard_normal(s, dtype=np.float32) * np.float32(0.02))
-    lw = dict(wq=nrm(H * D, h), wk=nrm(HK * D, h), wv=nrm(HK * D, h), wo=nrm(h, H * D), wg=nrm(F, h), wu=nrm(F, h),
-              wd=nrm(h, F), in_norm=np.ones(h, np.float32), post_norm=np.ones(h, np.float32),
-              q_norm=np.ones(D, np.float32), k_norm=np.ones(D, np.float32))
-    W = dict(embed=nrm(V // 28, h), lm_head=nrm(V // 28, h), final_norm=np.ones(h, np.float32), layers=[lw])
+    tree = build_trie(top_up(rng, chain_seqs(rng, 4, chain, V), nodes, V))
     cfg = dict(n_heads=H, n_kv_heads=HK, head_dim=D, rms_eps=1e-6, rope_theta=1e6)
-    tree = build_trie(top_up(rng, chain_seqs(rng, 4, chain, V // 28), nodes, V // 28))
-    kc = [round_bf16(rng.standard_normal((HK, prompt + nodes, D), dtype=np.float32))]
-    vc = [round_bf16(rng.standard_normal((HK, prompt + nodes, D), dtype=np.float32))]
-    # all host threads (torchrun sets OMP_NUM_THREADS=1 for its workers; the
-    # BLAS pool is raised explicitly and the count actually in use reported)
-    from threadpoolctl import threadpool_info, threadpool_limits
     times = []
-    with threadpool_limits(limits=os.cpu_count() or 1):
-        pools = [p["num_threads"] for p in threadpool_info()]
-        for i in range(warmup + steps):
-            t0 = time.perf_counter()
-            omodel.verify_step(W, cfg, tree.tokens(), tree.parents(), tree.depths(), prompt, 0, kc, vc)
-            if i >= warmup:
-                times.append(time.perf_counter() - t0)
-    t_step = 28 * statistics.median(times)
-    threads = max(pools) if pools else 1
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        tm.verify_step(W, cfg, tree.tokens(), tree.parents(), tree.depths(), prompt, 0, kc, vc, mode="eager")
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    t_step = sum(times) / len(times)
+    threads = torch.get_num_threads()
+    del W, kc, vc
     return dict(value=chain / t_step, unit="committed tokens/s", cores=threads, kind="port",
-                sample=("numpy oracle (oracle/model.py), one full-size decoder layer of the verify step "
-                        f"({nodes} trie rows vs a {prompt}-token prefix) plus 1/28 of the lm_head rows; "
-                        f"step time = 28 x median of {steps} samples = {t_step:.2f} s"),
-                ms_per_step=t_step * 1e3)
+                sample=(f"{steps} whole verify steps (after {warmup} untimed) of the reference's eager path in bf16 "
+                        f"on {threads} host threads (oracle/torch_model.py mode eager: the full 28-layer config-3 "
+                        f"model, {nodes} trie rows vs a {prompt}-token prefix, torch CPU ops); mean step "
+                        f"{t_step:.2f} s; {chain} committed tokens per step as on the GPU"),
+                ms_per_step=t_step * 1e3, steps=steps, warmup=warmup)
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    steps = max(1, min(args.steps, 3))
-    warm = max(0, min(args.warmup, 1))
-    cb = cpu_sample(steps, warm)
+    # whole steps of a few seconds each: at most 20 timed and 2 untimed, so the
+    # run stays within a couple of minutes on the host cores
+    steps = max(1, min(args.steps, 20))
+    warm = max(1, min(args.warmup, 2))
+    cb = cpu_steps(steps, warm)
     line = {"metric": "committed tokens/s (trie-verify step)", "value": cb["value"], "unit": cb["unit"],
             "impl": "reference", "n_gpus": args.gpus, "steps": steps, "warmup": warm,
             "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic (seeded)", "config": config_block(args.gpus),
+            "dtype": "bf16", "data": "synthetic (seeded)", "config": config_block(args.gpus),
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -364,7 +367,7 @@ def run_native(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cb = cpu_sample(2, 1, nodes=NODES, prompt=PROMPT)
+        cb = cpu_steps(2, 1, nodes=NODES, prompt=PROMPT)
         cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
     err = _lib.device_error()
     launches = args.steps * (KERNELS_FIXED + KERNELS_PER_LAYER * cfg.n_layers)
@@ -442,9 +445,10 @@ def run_frame_replay(args):
     d2h = (stats.rounds * 4 * (4 + 2 * rows) + frames * 8 * rcfg.prefill_chunk) / max(frames, 1)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        # the oracle's 256-row step at the 4096-token prefix, times the steps the timed
-        # frames ran (prefill chunks counted as full-prefix steps: an upper bound)
-        cb = cpu_sample(2, 1, nodes=rows, prompt=rcfg.prompt_len, chain=rcfg.chain_len)
+        # whole 256-row steps of the reference's eager path at the 4096-token prefix,
+        # times the steps the timed frames ran (prefill chunks counted as full-prefix
+        # steps: an upper bound)
+        cb = cpu_steps(2, 1, nodes=rows, prompt=rcfg.prompt_len, chain=rcfg.chain_len)
         cpu_frame_s = n_steps * cb["ms_per_step"] / 1e3 / max(frames, 1)
         cpu = {"value": 1.0 / cpu_frame_s, "unit": "frames/s", "cores": cb["cores"], "kind": "port",
                "sample": cb["sample"] + f"; a frame = {n_steps / max(frames, 1):.1f} such steps (the timed "

@@ -66,10 +66,11 @@ def _rot(x: torch.Tensor) -> torch.Tensor:
     return torch.cat([-x[..., h:], x[..., :h]], dim=-1)
 
 
-def _split_gate_up(wgu: torch.Tensor):
-    f2, h = wgu.shape
-    v = wgu.view(f2 // 256, 2, 128, h)
-    return v[:, 0].reshape(f2 // 2, h), v[:, 1].reshape(f2 // 2, h)
+def _split_gate_up(gu: torch.Tensor):
+    """x @ wgu^T [q, 2F] (gate and up in alternating 128-column blocks) -> gate, up [q, F]."""
+    q, f2 = gu.shape
+    v = gu.view(q, f2 // 256, 2, 128)
+    return v[:, :, 0].reshape(q, f2 // 2), v[:, :, 1].reshape(q, f2 // 2)
 
 
 # --------------------------------------------------------------------- fp32 mode
@@ -156,13 +157,12 @@ def verify_step(W: dict, cfg: dict, ids, parents, depths, prompt_len: int, base:
         kc[li][:, slots] = kh.to(kc[li].dtype)
         vc[li][:, slots] = vh.transpose(0, 1).to(vc[li].dtype)
         k_all, v_all = kc[li][:, :n_keys], vc[li][:, :n_keys]
-        wg, wu = _split_gate_up(lw["wgu"])
         if fp32:
             a = _attend32(qh, k_all.float(), v_all.float(), allow, scale)
             a = _round(a).transpose(0, 1).reshape(q, H * D)
             h = _round(h + _lin32(a, lw["wo"]))
             x = _norm32(h, lw["post_norm"], eps)
-            g, u = _lin32(x, wg), _lin32(x, wu)
+            g, u = _split_gate_up(_lin32(x, lw["wgu"]))
             act = _round(_round(g / (1.0 + torch.exp(-g))) * u)
             h = _round(h + _lin32(act, lw["wd"]))
         else:
@@ -171,7 +171,8 @@ def verify_step(W: dict, cfg: dict, ids, parents, depths, prompt_len: int, base:
             a = a[0].transpose(0, 1).reshape(q, H * D)
             h = h + a @ lw["wo"].T
             x = _norm16(h, lw["post_norm"], eps)
-            act = torch.nn.functional.silu(x @ wg.T) * (x @ wu.T)
+            g, u = _split_gate_up(x @ lw["wgu"].T)
+            act = torch.nn.functional.silu(g) * u
             h = h + act @ lw["wd"].T
     if fp32:
         return _lin32(_norm32(h, W["final_norm"], eps), W["lm_head"], out_bf16=False)
@@ -191,17 +192,15 @@ def cfg_of(c) -> dict:
 def random_weights_cpu(hidden, n_layers, n_heads, n_kv_heads, head_dim, ffn, vocab, seed=0, std=0.02) -> dict:
     """bf16 weights of that architecture on the host, ~N(0, std) elementwise, for
     timing only: each matrix's rows are seeded picks from the rows of one seeded
-    N(0, std) pool, rolled by a seeded shift (drawing 7e9 normals one by one takes
-    minutes on one core; a row gather runs at memory speed). Norm weights are 1,
-    as HF initialises them."""
+    N(0, std) pool (drawing 7e9 normals one by one takes minutes on one core; a
+    row gather runs at memory speed). Norm weights are 1, as HF initialises them."""
     g = torch.Generator().manual_seed(seed)
     pool = (torch.randn(1 << 24, generator=g) * std).to(torch.bfloat16)
 
     def mat(n, k):
         rows = pool[: pool.numel() - pool.numel() % k].view(-1, k)
         pick = torch.randint(0, rows.shape[0], (n,), generator=g)
-        shift = int(torch.randint(0, k, (1,), generator=g))
-        return torch.roll(rows[pick], shifts=shift, dims=1).contiguous()
+        return rows.index_select(0, pick)
 
     d = head_dim
     layers = []
