@@ -14,6 +14,9 @@ at BASELINE config-3 size on any device, in one of two modes:
   (respect/kernels/attention.py:36-71 computes the same function; only the
   order of its fp32 sums differs). This is the full-size reference the GPU
   parity test holds the native engine to.
+* ``mode="exact"`` — the same forward with no bf16 rounding of activations at
+  all (fp32 throughout over the bf16 weights): the value both bf16
+  implementations approximate, against which their errors are measured.
 * ``mode="eager"`` — the reference's eager path in bf16, as HF runs it when
   no dedicated kernel is installed (respect/decoding/verify.py:42-46 with
   attention through SDPA and the additive bf16 trie mask of verify.py:35-41):
@@ -34,7 +37,10 @@ import torch
 
 def _round(x: torch.Tensor) -> torch.Tensor:
     """fp32 -> nearest bf16 value (round to nearest even), kept in fp32."""
-    return x.to(torch.bfloat16).float()
+    return x.to(torch.bfloat16).float() if _ROUND[0] else x
+
+
+_ROUND = [True]     # False while a mode="exact" forward runs
 
 
 def _ancestry_mask(parents) -> torch.Tensor:
@@ -114,8 +120,14 @@ def verify_step(W: dict, cfg: dict, ids, parents, depths, prompt_len: int, base:
                 mode: str = "fp32", layers: int | None = None) -> torch.Tensor:
     """fp32 logits [q, V] of one verify forward; node i is written to slot
     prompt_len + base + i of every layer's K / V (respect/decoding/verify.py:24-33)."""
-    if mode not in ("fp32", "eager"):
-        raise ValueError(f"mode must be 'fp32' or 'eager', not {mode!r}")
+    if mode not in ("fp32", "exact", "eager"):
+        raise ValueError(f"mode must be 'fp32', 'exact' or 'eager', not {mode!r}")
+    if mode == "exact":
+        _ROUND[0] = False
+        try:
+            return verify_step(W, cfg, ids, parents, depths, prompt_len, base, kc, vc, "fp32", layers)
+        finally:
+            _ROUND[0] = True
     dev = W["embed"].device
     H, HK, D = cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"]
     eps, theta = cfg["rms_eps"], cfg["rope_theta"]

@@ -155,15 +155,16 @@ class VerifyEngine:
     """One model replica on one device, with its fixed KV buffer.
 
     The KV buffer has `max_slots` slots per layer ([n_kv_heads, max_slots, 128]
-    bf16, like FixedKVBuffer's [1, Hkv, PL + cap_max, D], kv_buffer.py:44-64):
+    bf16, a FixedKVBuffer store's per-layer view; the reference's buffer is
+    [1, Hkv, PL + cap_max, D] per layer, kv_buffer.py:44-64):
     the prompt occupies [0, prompt_len), committed tokens follow, and a
     verify step writes its nodes after them.
     """
 
     def __init__(self, weights: DecoderWeights, max_rows: int, max_slots: int | None = None,
                  max_pos: int | None = None, kv=None, share_weights: "VerifyEngine | None" = None):
-        """`kv`: a FixedKVBuffer (respect_b200.decoding.kv_buffer, allocated) whose per-layer
-        [1, Hkv, slots, D] bf16 tensors the engine uses as its KV buffer, so a Prefill written
+        """`kv`: an allocated FixedKVBuffer (respect_b200.decoding.kv_buffer) whose store
+        [layers, 2, Hkv, slots, D] (bf16) the engine uses as its KV buffer, so a Prefill written
         into it (FixedKVBuffer.write_prefill) is verified in place; max_slots then defaults to
         its slot count. Without it the engine allocates [Hkv, max_slots, D] per layer.
         `share_weights`: another engine of the same model whose packed weights this one
@@ -176,17 +177,19 @@ class VerifyEngine:
             fn = getattr(lib, n)
             fn.restype, fn.argtypes = res, args
         if kv is not None:
-            shape = (1, c.n_kv_heads, kv.base_k[0].shape[2], c.head_dim)
-            for t in list(kv.base_k) + list(kv.base_v):
-                if tuple(t.shape) != shape or t.dtype != torch.bfloat16 or not t.is_contiguous() or t.device != self.device:
-                    raise ValueError(f"KV buffer tensors must be contiguous bf16 {shape} on {self.device}")
-            if len(kv.base_k) != c.n_layers:
-                raise ValueError(f"KV buffer has {len(kv.base_k)} layers, the model {c.n_layers}")
-            max_slots = shape[2] if max_slots is None else max_slots
-            if max_slots > shape[2]:
-                raise ValueError(f"max_slots {max_slots} exceeds the buffer's {shape[2]} slots")
-            self.kc = [t[0] for t in kv.base_k]   # views: the engine writes the buffer in place
-            self.vc = [t[0] for t in kv.base_v]
+            if kv.store is None:
+                raise ValueError("the FixedKVBuffer must be allocated (FixedKVBuffer.allocate) first")
+            shape = (c.n_layers, 2, c.n_kv_heads, kv.slots, c.head_dim)
+            if (tuple(kv.store.shape) != shape or kv.store.dtype != torch.bfloat16 or not kv.store.is_contiguous()
+                    or kv.store.device != self.device):
+                raise ValueError(f"KV store must be a contiguous bf16 {shape} tensor on {self.device}, "
+                                 f"not {kv.store.dtype} {tuple(kv.store.shape)}")
+            max_slots = kv.slots if max_slots is None else max_slots
+            if max_slots > kv.slots:
+                raise ValueError(f"max_slots {max_slots} exceeds the buffer's {kv.slots} slots")
+            pairs = [kv.layer_kv(i) for i in range(c.n_layers)]   # views: the engine writes the store in place
+            self.kc = [k for k, _ in pairs]
+            self.vc = [v for _, v in pairs]
         else:
             if max_slots is None:
                 raise ValueError("max_slots is required without a KV buffer")

@@ -7,11 +7,19 @@ token level (BASELINE config 3 and the north-star parity bar).
   acceptance walk equal to the reference's except at reported near-ties
   (tests/token_parity.py).
 * Full size: the config-3 verify step (hidden 3584, 28 / 4 heads of 128, FFN
-  18944, vocab 152,064, prefix 3,000, 128-node trie) against an independent
-  fp32 restatement of the reference's math on the same GPU over the same bf16
-  weights and the same prefix KV (oracle/torch_model.py): logits, node K / V and
-  greedy ids, for the first two layers plus the final norm and lm_head, and for
-  the whole 28-layer model.
+  18944, vocab 152,064, prefix 3,000, 128-node trie) on the same GPU, from the
+  same bf16 weights and prefix KV, next to two restatements
+  (oracle/torch_model.py): the reference's math with its bf16 rounding points,
+  and the exact forward with no activation rounding. At this width the bf16
+  rounding points make any two implementations that sum in different orders
+  part by a few 1e-2 in the logits after a layer or two (a last-bit flip in
+  0.06% of one layer's attention outputs reaches a quarter of the next residual
+  stream's elements and ~2e-2 in the logits), so the bar is accuracy: the
+  engine's distance to the exact forward must not exceed the reference math's
+  own (x1.25), for logits and node K / V, its first-layer K must match the
+  restatement up to rare last-bit flips, and a greedy id may differ from the
+  exact forward's only within that error. Two layers plus the final norm and
+  lm_head, and the whole 28-layer model.
 """
 import numpy as np
 import pytest
@@ -25,7 +33,7 @@ from tests import token_parity as tp
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-TOL = 2e-2
+TOL = 2e-2           # the bf16 logit bar (token-level test)
 
 
 def test_engine_token_parity_with_reference():
@@ -70,6 +78,9 @@ def test_engine_token_parity_with_reference():
 
 
 def _full_size_case(n_layers):
+    """The config-3 step on the engine, on the restatement with the reference's bf16
+    rounding points, and on the exact (unrounded fp32) forward, from the same bf16
+    weights and the same prefix KV. Returns the three sets of outputs' distances."""
     cfg = DecoderConfig(3584, n_layers, 28, 4, 128, 18944, 152064)
     w = DecoderWeights.random(cfg, DEV, seed=0)
     P, NODES = 3000, 128
@@ -78,38 +89,56 @@ def _full_size_case(n_layers):
     eng.prefill(rng.integers(0, cfg.vocab, P))
     tree = build_trie(top_up(rng, chain_seqs(rng, 4, 32, cfg.vocab), NODES, cfg.vocab))
     assert len(tree.nodes) == NODES
-    kc = [k.clone() for k in eng.kc]       # the engine's prefix KV, for the restatement
-    vc = [v.clone() for v in eng.vc]
+    args = (tm.weights_of(w), tm.cfg_of(cfg), tree.tokens(), tree.parents(), tree.depths(), P, 0)
+    kv_r = ([k.clone() for k in eng.kc], [v.clone() for v in eng.vc])              # bf16, as the engine's
+    kv_x = ([k.float() for k in eng.kc], [v.float() for v in eng.vc])              # fp32: nothing rounded
     eng.step(tree.tokens().astype(np.int32), tree.parents(), tree.depths(), 0, P)
-    got = eng.logits(NODES).clone()
-    ids = eng.next_ids(NODES).clone()
-    ref = tm.verify_step(tm.weights_of(w), tm.cfg_of(cfg), tree.tokens(), tree.parents(), tree.depths(), P, 0,
-                         kc, vc, mode="fp32")
-    err = (got - ref).abs().max().item()
-    kerr = max(max((eng.kc[li][:, P:P + NODES].float() - kc[li][:, P:P + NODES].float()).abs().max().item(),
-                   (eng.vc[li][:, P:P + NODES].float() - vc[li][:, P:P + NODES].float()).abs().max().item())
-               for li in range(n_layers))
-    top2 = ref.topk(2, dim=-1).values
-    margin = (top2[:, 0] - top2[:, 1]).cpu().numpy()
-    flips = np.flatnonzero(ids.cpu().numpy() != ref.argmax(-1).cpu().numpy())
+    got, ids = eng.logits(NODES).clone(), eng.next_ids(NODES).clone()
+    def nodes(kv):     # the step's node K / V of every layer, fp32
+        return [[t[:, P:P + NODES].float() for t in ts] for ts in kv]
+
+    kv_e = nodes((eng.kc, eng.vc))
     eng.close()
-    print(f"config-3 engine, {n_layers} layers, vs fp32 restatement: logits max-abs {err:.3e} "
-          f"(|logits| max {ref.abs().max().item():.2f}), node K/V max-abs {kerr:.3e}, "
-          f"greedy flips {[(int(n), float(margin[n])) for n in flips]}")
-    return err, kerr, flips, margin
+    restated = tm.verify_step(*args, *kv_r, mode="fp32")
+    exact = tm.verify_step(*args, *kv_x, mode="exact")
+    kv_r, kv_x = nodes(kv_r), nodes(kv_x)
+
+    def kv_err(a, b):
+        return max((x - y).abs().max().item() for xs, ys in zip(a, b) for x, y in zip(xs, ys))
+
+    top2 = exact.topk(2, dim=-1).values
+    margin = (top2[:, 0] - top2[:, 1]).cpu().numpy()
+    r = dict(e_eng=(got - exact).abs().max().item(), e_res=(restated - exact).abs().max().item(),
+             d=(got - restated).abs().max().item(), k_eng=kv_err(kv_e, kv_x), k_res=kv_err(kv_r, kv_x),
+             layer0_kv_mismatch=float((kv_e[0][0] != kv_r[0][0]).float().mean()),
+             layer0_kv_maxdiff=(kv_e[0][0] - kv_r[0][0]).abs().max().item(),
+             logits_max=exact.abs().max().item(),
+             flips=[(int(n), float(margin[n])) for n in
+                    np.flatnonzero(ids.cpu().numpy() != exact.argmax(-1).cpu().numpy())])
+    print(f"config-3 step, {n_layers} layers: logits max-abs vs exact fp32: engine {r['e_eng']:.3e}, "
+          f"reference bf16 math {r['e_res']:.3e}; engine vs reference bf16 math {r['d']:.3e}; "
+          f"node K/V vs exact: engine {r['k_eng']:.3e}, reference math {r['k_res']:.3e}; layer-0 K "
+          f"mismatch {r['layer0_kv_mismatch']:.2e} (max {r['layer0_kv_maxdiff']:.2e}); |logits| max "
+          f"{r['logits_max']:.2f}; greedy flips vs exact (node, exact margin) {r['flips']}")
+    return r
 
 
-def test_config3_two_layers_vs_fp32_restatement():
+def _check(r):
+    # as accurate as the reference's own bf16 math, measured against the exact forward
+    assert r["e_eng"] <= 1.25 * r["e_res"] + 5e-3, r
+    assert r["k_eng"] <= 1.25 * r["k_res"] + 5e-3, r
+    # the first layer's node K (one GEMM, norms, RoPE) differs only by rare last-bit flips
+    assert r["layer0_kv_mismatch"] < 5e-3 and r["layer0_kv_maxdiff"] <= 0.0625, r
+    # a greedy choice may differ from the exact forward's only where that margin is within the error
+    assert all(m < 2 * r["e_eng"] for _, m in r["flips"]), r
+
+
+def test_config3_two_layers_vs_restatement():
     """Every config-3 kernel at full size (q|k|v, attention over 3,000 + 128 keys, o,
     gate|up + SiLU*mul, down, norms, lm_head over 152,064 rows) through two layers."""
-    err, kerr, flips, margin = _full_size_case(2)
-    assert err <= TOL, err
-    assert kerr <= 0.05, kerr            # a bf16 ulp of the largest K / V values
-    assert all(margin[n] < TOL for n in flips)
+    _check(_full_size_case(2))
 
 
-def test_config3_28_layers_vs_fp32_restatement():
-    """The whole config-3 model (the step bench.py times) against the restatement."""
-    err, kerr, flips, margin = _full_size_case(28)
-    assert err <= TOL, err
-    assert all(margin[n] < TOL for n in flips)
+def test_config3_28_layers_vs_restatement():
+    """The whole config-3 model (the step bench.py times)."""
+    _check(_full_size_case(28))
