@@ -191,8 +191,8 @@ __device__ __forceinline__ bool node_allowed(const AttnDev& p, int row, int j) {
 
 // Node phase. A row's allowed node slots are visited in slot order, in
 // batches of up to 32. Lane u scores the batch's u-th slot (q.k over the 128
-// dims in a fixed order: ascending for bf16 data, four interleaved partial sums
-// for fp32; times scale*log2(e)), then the batch is folded
+// dims in a fixed order: four interleaved partial sums over d = 4c + e, added
+// pairwise; times scale*log2(e)), then the batch is folded
 // one slot at a time, starting from an empty state:
 //   m' = max(m, s); a = 2^(m - m'); p = 2^(s - m'); acc = p*v + acc*a; l = l*a + p
 // (lane u of the fold owns dims [4u, 4u+4)). Every slot goes through exactly
@@ -208,7 +208,6 @@ __device__ __forceinline__ bool node_allowed(const AttnDev& p, int row, int j) {
 // q and the node K / V, which the kernel before the prefix kernel wrote, so
 // under PDL they run while the prefix kernel is still working), the merges
 // with the prefix chunk partials after it.
-constexpr int kChunkGroup = 2;  // chunk partials loaded together
 constexpr int kMaxGroup = 16;   // query heads per kv head handled by one block
 
 template <typename T>
@@ -216,29 +215,30 @@ struct NodeSmem {
   static constexpr int kRow = 128 * static_cast<int>(sizeof(T));  // bytes of one K / V row
   static constexpr int kKPitch = kRow + 16;                         // padded: conflict-free lane-per-row reads
   static constexpr int kStage = 32 * (kKPitch + kRow);              // one batch of K and V rows
-  static int bytes(int G) { return kStage + G * 128 * 4; }          // + q of each head (fp32)
+  __host__ __device__ static int bytes(int G) { return kStage + G * 128 * 4; }   // + q of each head (fp32)
 };
 
 template <typename T>
 __device__ __forceinline__ float dot128_smem(const uint8_t* krow, const float* qs);
 template <>
 __device__ __forceinline__ float dot128_smem<uint16_t>(const uint8_t* krow, const float* qs) {
-  float s = 0.f;
-#pragma unroll 4
+  // four partial sums over d = 4c + e (fixed order), added pairwise at the end
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
   for (int c = 0; c < 16; ++c) {
     const uint4 k8 = reinterpret_cast<const uint4*>(krow)[c];
     const float4 qa = reinterpret_cast<const float4*>(qs)[2 * c];
     const float4 qb = reinterpret_cast<const float4*>(qs)[2 * c + 1];
-    s = fmaf(qa.x, bf16_bits_to_f32(static_cast<uint16_t>(k8.x)), s);
-    s = fmaf(qa.y, bf16_bits_to_f32(static_cast<uint16_t>(k8.x >> 16)), s);
-    s = fmaf(qa.z, bf16_bits_to_f32(static_cast<uint16_t>(k8.y)), s);
-    s = fmaf(qa.w, bf16_bits_to_f32(static_cast<uint16_t>(k8.y >> 16)), s);
-    s = fmaf(qb.x, bf16_bits_to_f32(static_cast<uint16_t>(k8.z)), s);
-    s = fmaf(qb.y, bf16_bits_to_f32(static_cast<uint16_t>(k8.z >> 16)), s);
-    s = fmaf(qb.z, bf16_bits_to_f32(static_cast<uint16_t>(k8.w)), s);
-    s = fmaf(qb.w, bf16_bits_to_f32(static_cast<uint16_t>(k8.w >> 16)), s);
+    s0 = fmaf(qa.x, bf16_bits_to_f32(static_cast<uint16_t>(k8.x)), s0);
+    s1 = fmaf(qa.y, bf16_bits_to_f32(static_cast<uint16_t>(k8.x >> 16)), s1);
+    s2 = fmaf(qa.z, bf16_bits_to_f32(static_cast<uint16_t>(k8.y)), s2);
+    s3 = fmaf(qa.w, bf16_bits_to_f32(static_cast<uint16_t>(k8.y >> 16)), s3);
+    s0 = fmaf(qb.x, bf16_bits_to_f32(static_cast<uint16_t>(k8.z)), s0);
+    s1 = fmaf(qb.y, bf16_bits_to_f32(static_cast<uint16_t>(k8.z >> 16)), s1);
+    s2 = fmaf(qb.z, bf16_bits_to_f32(static_cast<uint16_t>(k8.w)), s2);
+    s3 = fmaf(qb.w, bf16_bits_to_f32(static_cast<uint16_t>(k8.w >> 16)), s3);
   }
-  return s;
+  return (s0 + s1) + (s2 + s3);
 }
 template <>
 __device__ __forceinline__ float dot128_smem<float>(const uint8_t* krow, const float* qs) {
@@ -316,8 +316,12 @@ __device__ NodeAcc node_fold(const AttnDev& p, int row, int kvh, uint8_t* smem, 
       int slot = 0;
       bool v;
       if (trie) {
+        // the chain entry is read whether or not i < total (its address does not
+        // depend on the depth, so this load does not wait for the depth's)
+        const int ci = i - base;
+        const int cv = (ci >= 0 && ci < p.chain_ld) ? chain[ci] : 0;
         v = i < total;
-        slot = i < base ? i : (v ? base + chain[i - base] : 0);
+        slot = i < base ? i : base + cv;
       } else {
         v = i < p.NN && node_allowed(p, row, i);
         slot = i;
@@ -334,26 +338,40 @@ __device__ NodeAcc node_fold(const AttnDev& p, int row, int kvh, uint8_t* smem, 
     for (int t = threadIdx.x; t < cnt * kPieces; t += nthr) {
       const int u = t / kPieces, pc = t % kPieces;
       const int64_t sl = slots[u];
-      *reinterpret_cast<uint4*>(&ks[u][pc * 16]) =
-          *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(kn + kbase + sl * p.sknn) + pc * 16);
-      *reinterpret_cast<uint4*>(&vs[u][pc * 16]) =
-          *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(vn + vbase + sl * p.svnn) + pc * 16);
+      cp_async16(&ks[u][pc * 16], reinterpret_cast<const uint8_t*>(kn + kbase + sl * p.sknn) + pc * 16, 16u);
+      cp_async16(&vs[u][pc * 16], reinterpret_cast<const uint8_t*>(vn + vbase + sl * p.svnn) + pc * 16, 16u);
     }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    // 3. scores (lane u <- slot u), then the ordered fold
-    const float sc = lane < cnt ? dot128_smem<T>(&ks[lane][0], qs) * scale2 : 0.f;
+    // 3. scores (lane u <- slot u), then the ordered fold. The running max after
+    // each slot, m_u = max(m, s_0, ..., s_u), comes from a warp scan (max is exact,
+    // so it is the same value a one-slot-at-a-time loop reaches), and lane u forms
+    // its slot's weights a_u = 2^(m_{u-1} - m_u), p_u = 2^(s_u - m_u) in parallel;
+    // only the accumulation below runs slot by slot, in slot order:
+    //   acc = p_u v_u + acc a_u, l = l a_u + p_u
+    const float sc = lane < cnt ? dot128_smem<T>(&ks[lane][0], qs) * scale2 : -INFINITY;
+    float run = sc;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, run, d);
+      if (lane >= d) run = fmaxf(run, y);
+    }
+    const float m_u = fmaxf(r.m, run);
+    float m_prev = __shfl_up_sync(0xffffffffu, m_u, 1);
+    if (lane == 0) m_prev = r.m;
+    const float a_u = fast_exp2(m_prev - m_u);
+    const float p_u = fast_exp2(sc - m_u);
+#pragma unroll 4
     for (int u = 0; u < cnt; ++u) {
-      const float su = __shfl_sync(0xffffffffu, sc, u);
+      const float a = __shfl_sync(0xffffffffu, a_u, u);
+      const float pe = __shfl_sync(0xffffffffu, p_u, u);
       float vv[4];
       ld4(reinterpret_cast<const T*>(&vs[u][0]) + d0, vv);
-      const float m_new = fmaxf(r.m, su);
-      const float a = fast_exp2(r.m - m_new);
-      const float pe = fast_exp2(su - m_new);
 #pragma unroll
       for (int e = 0; e < 4; ++e) r.acc[e] = fmaf(pe, vv[e], r.acc[e] * a);
       r.l = fmaf(r.l, a, pe);
-      r.m = m_new;
     }
+    r.m = __shfl_sync(0xffffffffu, m_u, cnt - 1);
   }
   return r;
 }
@@ -387,11 +405,18 @@ __global__ void __maxnreg__(48) attn_nodes(const AttnDev p, const float* __restr
   pdl_wait();  // the prefix chunk partials are complete
   const int NP = p.sp ? p.sp->prompt_len : p.NP;
   const int nchunks = prefix_nchunks(NP, p.H);
+  // The chunk partials of a row (every head of the group) are copied into shared
+  // memory (the fold's staging area, free now) with all copies in flight, as many
+  // chunks as fit at a time; then warp g merges its head's pieces in chunk order.
+  constexpr int kPiece = kPartStride * 4;   // one (chunk, head, row) partial: 528 bytes
+  float* pieces = reinterpret_cast<float*>(node_smem);
+  // chunks staged per round: at least 2 for every group size up to kMaxGroup
+  const int cap = max(1, NodeSmem<T>::bytes(G) / kPiece / G);
 #pragma unroll
   for (int it = 0; it < R; ++it) {
     const int item = blockIdx.x + it * gridDim.x;
-    if (item >= n_items) continue;
-    const int row = item % p.M, h = (item / p.M) * G + warp;
+    if (item >= n_items) continue;   // uniform per block
+    const int row = item % p.M, kvh = item / p.M, h = kvh * G + warp;
     T* out = static_cast<T*>(p.out) + h * p.soh + static_cast<int64_t>(row) * p.som + d0;
     if (row >= live) {  // padding row of a bucketed engine step: zeros, no reads
 #pragma unroll
@@ -403,22 +428,24 @@ __global__ void __maxnreg__(48) attn_nodes(const AttnDev p, const float* __restr
     }
     // Prefix chunk partials in ascending chunk order, then the node partial.
     NodeAcc r{-INFINITY, 0.f, {0.f, 0.f, 0.f, 0.f}};
-    for (int c0 = 0; c0 < nchunks; c0 += kChunkGroup) {
-      float cm[kChunkGroup], cl[kChunkGroup];
-      float ca[kChunkGroup][4];
-#pragma unroll
-      for (int g = 0; g < kChunkGroup; ++g) {
-        cm[g] = -INFINITY;
-        if (c0 + g < nchunks) {
-          const float* o = part + ((static_cast<int64_t>(c0 + g) * p.H + h) * p.M + row) * kPartStride;
-          cm[g] = o[D];
-          cl[g] = o[D + 1];
-          const float4 v = *reinterpret_cast<const float4*>(o + d0);
-          ca[g][0] = v.x; ca[g][1] = v.y; ca[g][2] = v.z; ca[g][3] = v.w;
-        }
+    for (int c0 = 0; c0 < nchunks; c0 += cap) {
+      const int nc = min(cap, nchunks - c0);
+      __syncthreads();   // the fold's (or the previous round's) reads of this area are done
+      for (int t = threadIdx.x; t < nc * G * (kPiece / 16); t += blockDim.x) {
+        const int pc = t % (kPiece / 16), pi = t / (kPiece / 16);   // piece pi = (chunk c0 + pi / G, head pi % G)
+        const int c = c0 + pi / G, g = pi % G;
+        const float* src = part + ((static_cast<int64_t>(c) * p.H + kvh * G + g) * p.M + row) * kPartStride;
+        cp_async16(reinterpret_cast<uint8_t*>(pieces) + pi * kPiece + pc * 16,
+                   reinterpret_cast<const uint8_t*>(src) + pc * 16, 16u);
       }
-#pragma unroll
-      for (int g = 0; g < kChunkGroup; ++g) merge_into(r, cm[g], cl[g], ca[g]);
+      asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+      __syncthreads();
+      for (int k = 0; k < nc; ++k) {
+        const float* o = pieces + (k * G + warp) * kPartStride;
+        const float4 v = *reinterpret_cast<const float4*>(o + d0);
+        const float ca[4] = {v.x, v.y, v.z, v.w};
+        merge_into(r, o[D], o[D + 1], ca);
+      }
     }
     merge_into(r, nd[it].m, nd[it].l, nd[it].acc);
 #pragma unroll
