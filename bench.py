@@ -21,6 +21,10 @@ barrier and the max over ranks is reported.
 steps of its eager bf16 forward at the config-3 model size (a torch restatement,
 oracle/torch_model.py), at most 20 timed steps.
 
+The default line also carries `frame_replay`: config 5 measured in the same run
+(16 frame streams per GPU, one untimed and --replay-frames timed frames each;
+--replay-frames 0 leaves it out), so a run at N GPUs records frames/s at N.
+
 --workload frame_replay [--streams S]: the multi-stream frame replay (S frame
 streams per GPU, 4,096-token prompts, 256-node tries, 80 committed tokens per
 frame); --warmup / --steps count frames per stream (defaults 1 / 2); metric
@@ -78,6 +82,9 @@ def parse():
                     help="frame_replay: all frame streams' work on one CUDA stream")
     ap.add_argument("--nodes", type=int, default=NODES, help="verify_step: trie nodes (config 3: 128)")
     ap.add_argument("--prefix", type=int, default=PROMPT, help="verify_step: prompt tokens (config 3: 3000)")
+    ap.add_argument("--replay-frames", type=int, default=1,
+                    help="verify_step: timed frames per stream of the frame replay carried in the line (0: none)")
+    ap.add_argument("--replay-streams", type=int, default=16)
     args = ap.parse_args()
     replay = args.workload == "frame_replay" and not args.kernel_case
     if args.steps is None:
@@ -365,6 +372,22 @@ def run_native(args):
                  "peak": hbm, "unit": "GB/s", "frac": step_bytes / (ms_step * 1e-3) / 1e9 / hbm,
                  "floor_ms": step_bytes / (hbm * 1e9) * 1e3}
 
+    # config 5 beside it: the multi-stream frame replay on this GPU (weights shared with
+    # the config-3 engine), so every run, the scaling runs included, records frames/s
+    replay = None
+    if args.replay_frames > 0:
+        r = replay_measure(w, world, rank, local, dev, args.replay_streams, 1, args.replay_frames, share=eng)
+        st = r["stats"]
+        replay = {"metric": "frames/s (multi-stream frame replay, config 5)", "value": r["value"],
+                  "unit": "frames/s", "n_gpus": world, "scaling": "weak", "streams_per_gpu": args.replay_streams,
+                  "warmup_frames_per_stream": 1, "frames_per_stream": args.replay_frames, "ms": r["ms"],
+                  "frames": r["frames"], "rounds": st.rounds, "prefill_steps": st.prefill_steps,
+                  "tokens_per_round": st.tokens_per_round(), "ms_per_step": r["ms"] / max(r["n_steps"], 1),
+                  "floor_frac": r["roofline"]["frac"], "step_floor_ms": r["roofline"]["step_floor_ms"],
+                  "bound": r["roofline"]["bound"], "clocks": r["clocks"],
+                  "workload": "16 frame streams per GPU, 4096-token prompts 90% shared with the previous frame, "
+                              "256-node tries, 80 committed tokens per frame; one untimed frame per stream, "
+                              "then the timed frames, max over ranks"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_steps(2, 1, nodes=NODES, prompt=PROMPT)
@@ -377,7 +400,7 @@ def run_native(args):
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded ids, random-init weights)", "config": config_block(world, NODES, PROMPT),
                 "e2e": e2e, "gpu_launches": launches, "roofline": roof, "step_roofline": step_roof,
-                "cpu_baseline": cpu, "clocks": clocks, "device_error": err}
+                "cpu_baseline": cpu, "clocks": clocks, "frame_replay": replay, "device_error": err}
         print(json.dumps(line), flush=True)
     eng.close()
     if world > 1:
@@ -386,42 +409,34 @@ def run_native(args):
 
 
 # ------------------------------------------------------------------ frame replay
-def run_frame_replay(args):
-    """Multi-stream frame replay: --streams frame streams per GPU (16 by default),
-    each frame a 4,096-token prompt (90% shared with the previous frame, Prefill
-    reusing the unchanged chunks) and 256-node verification rounds until 80 tokens
-    are committed. --warmup frames per stream untimed, then --steps frames per
-    stream timed. Metric: frames/s (whole job)."""
-    import torch
+def replay_measure(w, world, rank, local, dev, streams, warm_frames, frames_per_stream, one_cuda_stream=False,
+                   share=None):
+    """The config-5 frame replay on this rank's GPU: `streams` frame streams (one
+    VerifyEngine each on shared weights; `share`: an engine of the same weights whose
+    packed copy they reuse), `warm_frames` untimed frames per stream, then
+    `frames_per_stream` timed ones between CUDA events (all ranks start together;
+    the max over ranks is taken). Returns the measurement and its floor."""
     import torch.distributed as dist
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=dev)
-
-    from respect_b200 import _lib
-    from respect_b200.decoding.engine import DecoderConfig, DecoderWeights
+    from respect_b200.decoding.engine import VerifyEngine
     from respect_b200.decoding.replay import FrameReplay, ReplayConfig
-
-    cfg = DecoderConfig.baseline_7b()
-    w = DecoderWeights.random(cfg, dev, seed=0)
-    rcfg = ReplayConfig(streams=args.streams, seed=1000 + rank, shared_cuda_stream=args.one_cuda_stream)
-    rep = FrameReplay(w, rcfg)
-    warm = rep.run(args.warmup)
+    cfg = w.cfg
+    rcfg = ReplayConfig(streams=streams, seed=1000 + rank, shared_cuda_stream=one_cuda_stream)
+    engines = None
+    if share is not None:
+        rows = max(rcfg.trie_nodes, rcfg.prefill_chunk)
+        engines = [VerifyEngine(w, max_rows=rows, max_slots=rcfg.max_slots(), share_weights=share)
+                   for _ in range(streams)]
+    rep = FrameReplay(w, rcfg, engines=engines)
+    warm = rep.run(warm_frames)
     if world > 1:
         dist.barrier()
     with Clocks(local) as clk:
-        stats, ms = rep.timed_run(args.steps)
+        stats, ms = rep.timed_run(frames_per_stream)
     ms = reduce_max(ms, dev)
     clocks = clk.summary()
     frames = stats.frames
     value = world * frames / (ms / 1e3)
-
     # floor of the steps the timed frames ran (prefill chunks and verification
     # rounds, 256 rows each): max(HBM bytes / peak, tensor FLOPs / peak) per step
     hbm, tf, src = measured_peaks()
@@ -443,6 +458,37 @@ def run_frame_replay(args):
     per_round = 32 + 3 * 4 * rows
     h2d = (stats.prefill_tokens * 12 + stats.prefill_steps * 32 + stats.rounds * per_round) / max(frames, 1)
     d2h = (stats.rounds * 4 * (4 + 2 * rows) + frames * 8 * rcfg.prefill_chunk) / max(frames, 1)
+    rep.close()
+    return dict(rcfg=rcfg, stats=stats, warm=warm, ms=ms, value=value, clocks=clocks, frames=frames, rows=rows,
+                n_steps=n_steps, roofline=roof, h2d=h2d, d2h=d2h)
+
+
+def run_frame_replay(args):
+    """Multi-stream frame replay: --streams frame streams per GPU (16 by default),
+    each frame a 4,096-token prompt (90% shared with the previous frame, Prefill
+    reusing the unchanged chunks) and 256-node verification rounds until 80 tokens
+    are committed. --warmup frames per stream untimed, then --steps frames per
+    stream timed. Metric: frames/s (whole job)."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=dev)
+
+    from respect_b200 import _lib
+    from respect_b200.decoding.engine import DecoderConfig, DecoderWeights
+
+    cfg = DecoderConfig.baseline_7b()
+    w = DecoderWeights.random(cfg, dev, seed=0)
+    r = replay_measure(w, world, rank, local, dev, args.streams, args.warmup, args.steps, args.one_cuda_stream)
+    rcfg, stats, ms, value, clocks = r["rcfg"], r["stats"], r["ms"], r["value"], r["clocks"]
+    frames, rows, n_steps, roof, h2d, d2h = r["frames"], r["rows"], r["n_steps"], r["roofline"], r["h2d"], r["d2h"]
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         # whole 256-row steps of the reference's eager path at the 4096-token prefix,
@@ -475,10 +521,9 @@ def run_frame_replay(args):
                 "replay": {"frames": frames, "rounds": stats.rounds, "committed": stats.committed,
                            "tokens_per_round": stats.tokens_per_round(), "prefill_steps": stats.prefill_steps,
                            "prefill_tokens_per_frame": stats.prefill_tokens / max(frames, 1),
-                           "warmup_frames": warm.frames},
+                           "warmup_frames": r["warm"].frames},
                 "clocks": clocks, "device_error": err}
         print(json.dumps(line), flush=True)
-    rep.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
