@@ -42,6 +42,11 @@ kernel on a small footprint; prints one JSON line with the per-launch time.
                 two layers' packed weights (0.54 GB) used alternately.
   attention:    one layer's trie attention, 28/4 heads, 3000-key prefix,
                 128-node trie, bf16.
+  step_small:   the verify step of a ONE-layer decoder of config-3 width (every
+                kernel of a config-3 layer plus the 152,064-row lm_head at its
+                config-3 shape, about 4 GB on the device): the engine prefills
+                the --prefix prompt in 128-row chunks, then runs --steps graph
+                replays of the --nodes-row step; for per-kernel profiles.
 """
 from __future__ import annotations
 
@@ -75,7 +80,8 @@ def parse():
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel-case", default=None, choices=["gemm_gate_up", "attention", "config1", "config2"])
+    ap.add_argument("--kernel-case", default=None,
+                    choices=["gemm_gate_up", "attention", "config1", "config2", "step_small"])
     ap.add_argument("--workload", default="verify_step", choices=["verify_step", "frame_replay"])
     ap.add_argument("--streams", type=int, default=16)
     ap.add_argument("--one-cuda-stream", action="store_true",
@@ -118,7 +124,7 @@ def config_block(n, nodes=NODES, prompt=PROMPT):
     name = "config3: " if (nodes, prompt) == (NODES, PROMPT) else ""
     return {"workload": f"{name}trie verify step, 28-layer 7B-class decoder, prefix {prompt}, {nodes}-node trie",
             "model": "qwen3-style random-init hidden3584 L28 H28/4 D128 F18944 V152064",
-            "prefix": prompt, "trie_nodes": nodes, "committed_per_step": CHAIN, "global_batch": n,
+            "prefix": prompt, "trie_nodes": nodes, "committed_per_step": min(CHAIN, nodes), "global_batch": n,
             "parallelism": f"replicas{n}", "l2": "inputs larger than L2 (14.1 GB weights per step)"}
 
 
@@ -275,13 +281,16 @@ def run_native(args):
     # the model's own greedy continuation (1-token steps) becomes one chain
     first = int(rng.integers(0, cfg.vocab))
     toks = [first]
-    for t in range(CHAIN):
+    chain_n = min(CHAIN, NODES)   # the AR chain (32 tokens at config 3) fits the trie
+    for t in range(chain_n):
         eng.step(np.array([toks[-1]], np.int32), np.array([-1], np.int32), np.array([0], np.int32), t, PROMPT)
         toks.append(int(eng.fetch_ids(1)[0]))
-    seqs = [tuple(toks[:CHAIN])]
-    while len(seqs) < 4:
-        share = int(rng.integers(1, CHAIN))
-        cand = tuple(toks[:share]) + tuple(int(x) for x in rng.integers(0, cfg.vocab, CHAIN - share))
+    seqs = [tuple(toks[:chain_n])]
+    for _ in range(64):   # up to 3 more chains sharing a seeded prefix with it, while they fit
+        if len(seqs) == 4 or chain_n < 2:
+            break
+        share = int(rng.integers(1, chain_n))
+        cand = tuple(toks[:share]) + tuple(int(x) for x in rng.integers(0, cfg.vocab, chain_n - share))
         if len(build_trie(seqs + [cand]).nodes) <= NODES:
             seqs.append(cand)
     tree = build_trie(top_up(rng, seqs, NODES, cfg.vocab))
@@ -298,7 +307,7 @@ def run_native(args):
     am = eng.verify(tree, PROMPT, 0)
     path, acc, rec = walk(tree, first, 1 << 30, -1, lambda a, ch: int(am[ch]))
     committed = len(acc)
-    assert acc == toks[:CHAIN] and committed == CHAIN, "trie verify disagrees with AR decoding"
+    assert acc == toks[:chain_n] and committed == chain_n, "trie verify disagrees with AR decoding"
 
     for _ in range(args.warmup):
         device_step()
@@ -671,7 +680,25 @@ def run_kernel_case(args):
     NODES, PROMPT = args.nodes, args.prefix  # noqa: N806 (config 3: 128, 3000)
     g = torch.Generator(device=dev).manual_seed(7)
     st = torch.cuda.current_stream(dev)
-    if args.kernel_case == "gemm_gate_up":
+    if args.kernel_case == "step_small":
+        from oracle.inputs import chain_seqs, top_up
+        from respect_b200.candidates.trie import build_trie
+        from respect_b200.decoding.engine import DecoderWeights, VerifyEngine
+        c1 = DecoderConfig(cfg.hidden, 1, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab)
+        w = DecoderWeights.random(c1, dev, seed=0)
+        eng = VerifyEngine(w, max_rows=NODES, max_slots=PROMPT + 1024)
+        rng = np.random.default_rng(100)
+        eng.prefill(rng.integers(0, c1.vocab, PROMPT))
+        tree = build_trie(top_up(rng, chain_seqs(rng, 4, 32, c1.vocab), NODES, c1.vocab))
+        ids_d = torch.from_numpy(tree.tokens().astype(np.int32)).to(dev)
+        par_d = torch.from_numpy(tree.parents()).to(dev)
+        dep_d = torch.from_numpy(tree.depths()).to(dev)
+
+        def launch(i):
+            eng.step(ids_d, par_d, dep_d, 0, PROMPT)
+        algo = c1.weight_bytes_per_step()
+        flops = 2 * NODES * (c1.layer_params() + c1.vocab * c1.hidden)
+    elif args.kernel_case == "gemm_gate_up":
         from respect_b200.kernels.gemm import linear_swiglu_packed, pack_gate_up
         h, F = cfg.hidden, cfg.ffn
         ws = []
