@@ -105,14 +105,16 @@ RB_API int rb_fused_attn_hyb(const rb_attn_args* a, void* workspace, size_t ws_b
 
 /* The same attention for callers that cannot allocate device memory (no
  * cudaMalloc allowed where they run, or only their inputs and outputs in hand):
- * the scratch lives in a 4 MiB array of device memory owned by the library, one
+ * the scratch lives in a 16 MiB array of device memory owned by the library, one
  * per GPU that loads it, kept until the process exits. This entry point itself
  * allocates nothing. No counterpart in the reference (its Triton kernel needs
  * no scratch).
- *  - Calls needing more than 4 MiB of scratch (rb_fused_attn_hyb_workspace)
+ *  - Calls needing more than 16 MiB of scratch (rb_fused_attn_hyb_workspace)
  *    return RB_ERR_CAPACITY.
- *  - The first call on a device looks up the array's device address (with that
- *    device current); make it before capturing a stream into a CUDA graph.
+ *  - The array's address is looked up in the caller's current CUDA context the
+ *    first time the entry point runs there (a primary context, a context the
+ *    caller created, a context re-created after a device reset); make that first
+ *    call before capturing a stream into a CUDA graph.
  *  - All calls share the one array: calls that may overlap on the GPU (different
  *    streams, concurrent graphs) race on it and must be serialised by the caller.
  *  - The array keeps the last call's contents; nothing in it needs to start at zero. */

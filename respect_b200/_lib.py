@@ -16,6 +16,7 @@ import torch
 LIB_PATH = Path(os.environ.get("RESPECT_B200_LIB") or Path(__file__).resolve().parent / "librespect_b200.so")
 
 RB_OK = 0
+RB_ERR_INVALID_ARG, RB_ERR_UNSUPPORTED, RB_ERR_CAPACITY, RB_ERR_CUDA, RB_ERR_DEVICE_TIMEOUT, RB_ERR_WORKSPACE = 1, 2, 3, 4, 5, 6
 RB_F32, RB_BF16, RB_U8, RB_I32, RB_I64 = 0, 1, 2, 3, 4
 RB_MASK_BOOL, RB_MASK_ADD_BF16, RB_MASK_ADD_F32, RB_MASK_CAUSAL = 0, 1, 2, 3
 COMPACT_MAX_LAYERS = 128
