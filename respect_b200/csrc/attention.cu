@@ -457,6 +457,294 @@ __global__ void __maxnreg__(48) attn_nodes(const AttnDev p, const float* __restr
   }
 }
 
+// ----------------------------------------------------------------- node phase, bf16 (tensor cores)
+// One warp per item (query row x kv head) folds the row's ordered key list (the
+// committed slots, then its trie ancestors root first; in the mask modes, the
+// allowed slots in slot order) for all G query heads of the kv head at once, in
+// batches of 32 list entries counted from the start of the list:
+//   S = Q K_list^T          mma.sync m16n8k16 (heads padded to 16 rows), fp32
+//   m' = max(m, rowmax(S*scale)); a = 2^(m - m'); P = 2^(S*scale - m')
+//   O = O*a + bf16(P) V_list   mma.sync, fp32 accumulators; l = l*a + rowsum(P)
+// The MMAs group keys by their position in that list, never by their slot in
+// the KV buffer, and a trie node's list is the same sequence as the token-by-token
+// step's (its committed keys), so a committed row gets the same bits either way.
+// Row maxima and sums combine the four threads of a quad by shuffles in a fixed
+// order. After griddepcontrol.wait the node partial is merged with the prefix
+// chunk partials (chunk order, node partial last), as in attn_nodes.
+namespace nm {
+constexpr int kPitch = 136;                       // bf16 elements per staged row (272 bytes: ldmatrix conflict-free)
+constexpr int kQRows = 16, kListRows = 32;
+constexpr int kQBytes = kQRows * kPitch * 2;      // 4352
+constexpr int kKVBytes = kListRows * kPitch * 2;  // 8704 each for K and V
+constexpr int kStageBytes = kQBytes + 2 * kKVBytes;
+__host__ __device__ inline int smem_bytes(int G) { return kStageBytes + G * kPartStride * 4 + kListRows * 4; }
+}  // namespace nm
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+// d (16x8 fp32) += a (16x16 bf16, row-major) * b (16x8 bf16, column-major)
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(32) attn_nodes_mma(const AttnDev p, const float* __restrict__ part) {
+  using namespace nm;
+  extern __shared__ __align__(16) uint8_t nsm[];
+  uint16_t* Qs = reinterpret_cast<uint16_t*>(nsm);
+  uint16_t* Ks = reinterpret_cast<uint16_t*>(nsm + kQBytes);
+  uint16_t* Vs = reinterpret_cast<uint16_t*>(nsm + kQBytes + kKVBytes);
+  const int G = p.H / p.HK;
+  float* npart = reinterpret_cast<float*>(nsm + kStageBytes);                   // [G][kPartStride]
+  int* slots = reinterpret_cast<int*>(nsm + kStageBytes + G * kPartStride * 4);  // [kListRows]
+  const int lane = threadIdx.x, g = lane >> 2, c = lane & 3;
+  const int live = p.sp ? p.sp->q : p.M;
+  const int row = blockIdx.x % p.M, kvh = blockIdx.x / p.M;
+  pdl_trigger();
+  for (int h = lane; h < G; h += 32) npart[h * kPartStride + 128] = -INFINITY;   // empty node partial
+
+  if (row < live) {
+    // ---- the node fold (needs only q and the node K / V: runs before the wait)
+    const int NP = p.sp ? p.sp->prompt_len : p.NP;
+    const uint16_t* kn = p.kn ? static_cast<const uint16_t*>(p.kn)
+                              : static_cast<const uint16_t*>(p.kp) + static_cast<int64_t>(NP) * p.skpn;
+    const uint16_t* vn = p.vn ? static_cast<const uint16_t*>(p.vn)
+                              : static_cast<const uint16_t*>(p.vp) + static_cast<int64_t>(NP) * p.svpn;
+    const int64_t kbase = static_cast<int64_t>(kvh) * p.sknh, vbase = static_cast<int64_t>(kvh) * p.svnh;
+    const bool trie = p.mask_kind == kMaskTrie;
+    int base = 0, depth = -1;
+    const int32_t* chain = nullptr;
+    if (trie) {
+      base = p.sp ? p.sp->base : p.causal_first;
+      depth = p.depths[row];
+      if (depth < 0 || depth > row || depth >= p.chain_ld) depth = -1;  // invalid trie: reported when the chain was built
+      chain = p.chain + static_cast<int64_t>(row) * p.chain_ld;
+    }
+    // q rows of the group's heads (8-byte pieces; rows past G are zero)
+    const uint16_t* q = static_cast<const uint16_t*>(p.q);
+    for (int i = lane; i < kQRows * 32; i += 32) {
+      const int r = i >> 5, pc = i & 31;
+      uint2 v = make_uint2(0u, 0u);
+      if (r < G) v = *reinterpret_cast<const uint2*>(q + (kvh * G + r) * p.sqh + static_cast<int64_t>(row) * p.sqm + pc * 4);
+      *reinterpret_cast<uint2*>(Qs + r * kPitch + pc * 4) = v;
+    }
+    float o[16][4];
+#pragma unroll
+    for (int d = 0; d < 16; ++d)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[d][e] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;   // query heads g and g + 8
+    const float scale2 = p.sm_scale * kLog2e;
+    const int total = trie ? base + depth + 1 : p.NN;
+    const uint32_t sQ = smem_u32(Qs), sK = smem_u32(Ks), sV = smem_u32(Vs);
+    // Batches are cut at fixed positions of the row's key list (every 32 list
+    // entries from its start), whatever slots the entries occupy: the candidates
+    // (list positions in trie mode, slots in the mask modes) are scanned in order
+    // and the allowed ones appended to slots[] until 32 are held or none remain.
+    int scan = 0;   // next candidate to examine
+    while (scan < total) {
+      // 1. the next (up to) 32 list entries
+      int cnt = 0;
+      __syncwarp();   // the previous batch's reads of slots / K / V are done (and q is staged)
+      while (cnt < kListRows && scan < total) {
+        const int i = scan + lane;
+        int slot = 0;
+        bool v;
+        if (trie) {
+          const int ci = i - base;
+          const int cv = (ci >= 0 && ci < p.chain_ld) ? chain[ci] : 0;
+          v = i < total;
+          slot = i < base ? i : base + cv;
+        } else {
+          v = i < total && node_allowed(p, row, i);
+          slot = i;
+        }
+        const unsigned bits = __ballot_sync(0xffffffffu, v);
+        const int rank = __popc(bits & ((1u << lane) - 1u)), room = kListRows - cnt;
+        if (v && rank < room) slots[cnt + rank] = slot;
+        const int n = __popc(bits);
+        if (n <= room) {
+          cnt += n;
+          scan += 32;
+        } else {   // the window holds more than fits: resume at its first entry left out
+          const unsigned left = __ballot_sync(0xffffffffu, v && rank == room);
+          scan += __ffs(left) - 1;
+          cnt = kListRows;
+        }
+      }
+      __syncwarp();
+      if (cnt == 0) break;
+      // 2. stage the entries' K and V rows (rows past cnt zero-filled)
+      for (int it = 0; it < kListRows / 2; ++it) {
+        const int u = it * 2 + (lane >> 4), pc = lane & 15;
+        const bool ok = u < cnt;
+        const int64_t sl = ok ? slots[u] : 0;
+        cp_async16(Ks + u * kPitch + pc * 8, kn + kbase + sl * p.sknn + pc * 8, ok ? 16u : 0u);
+        cp_async16(Vs + u * kPitch + pc * 8, vn + vbase + sl * p.svnn + pc * 8, ok ? 16u : 0u);
+      }
+      asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+      __syncwarp();
+      // 3. S = Q K^T over the 32 entries (four 8-entry tiles)
+      float sc[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[j][e] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        const int qr = (lane & 7) + ((lane >> 3) & 1) * 8, qc = kk * 16 + (lane >> 4) * 8;
+        ldsm_x4(sQ + (qr * kPitch + qc) * 2, a0, a1, a2, a3);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t b0r, b1r;
+          const int kr = j * 8 + (lane & 7), kc = kk * 16 + ((lane >> 3) & 1) * 8;
+          ldsm_x2(sK + (kr * kPitch + kc) * 2, b0r, b1r);
+          mma_bf16_16816(sc[j], a0, a1, a2, a3, b0r, b1r);
+        }
+      }
+      // 4. online softmax of rows g and g + 8 (entries past cnt masked)
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          if (j * 8 + 2 * c + e >= cnt) sc[j][e] = sc[j][2 + e] = -INFINITY;
+          mx0 = fmaxf(mx0, sc[j][e]);
+          mx1 = fmaxf(mx1, sc[j][2 + e]);
+        }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float n0 = fmaxf(m0, mx0 * scale2), n1 = fmaxf(m1, mx1 * scale2);
+      const float al0 = fast_exp2(m0 - n0), al1 = fast_exp2(m1 - n1);
+      float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          sc[j][e] = fast_exp2(fmaf(sc[j][e], scale2, -n0));
+          sc[j][2 + e] = fast_exp2(fmaf(sc[j][2 + e], scale2, -n1));
+          rs0 += sc[j][e];
+          rs1 += sc[j][2 + e];
+        }
+      rs0 += __shfl_xor_sync(0xffffffffu, rs0, 1);
+      rs0 += __shfl_xor_sync(0xffffffffu, rs0, 2);
+      rs1 += __shfl_xor_sync(0xffffffffu, rs1, 1);
+      rs1 += __shfl_xor_sync(0xffffffffu, rs1, 2);
+      l0 = fmaf(l0, al0, rs0);
+      l1 = fmaf(l1, al1, rs1);
+      m0 = n0;
+      m1 = n1;
+#pragma unroll
+      for (int d = 0; d < 16; ++d) {
+        o[d][0] *= al0; o[d][1] *= al0;
+        o[d][2] *= al1; o[d][3] *= al1;
+      }
+      // 5. O += bf16(P) V over the 32 entries (two 16-entry k-steps)
+      uint32_t pa[2][4];
+#pragma unroll
+      for (int kc = 0; kc < 2; ++kc) {
+        pa[kc][0] = pack_bf16x2(sc[2 * kc][0], sc[2 * kc][1]);
+        pa[kc][1] = pack_bf16x2(sc[2 * kc][2], sc[2 * kc][3]);
+        pa[kc][2] = pack_bf16x2(sc[2 * kc + 1][0], sc[2 * kc + 1][1]);
+        pa[kc][3] = pack_bf16x2(sc[2 * kc + 1][2], sc[2 * kc + 1][3]);
+      }
+#pragma unroll
+      for (int d = 0; d < 16; ++d)
+#pragma unroll
+        for (int kc = 0; kc < 2; ++kc) {
+          uint32_t b0r, b1r;
+          ldsm_x2_t(sV + ((kc * 16 + (lane & 15)) * kPitch + d * 8) * 2, b0r, b1r);
+          mma_bf16_16816(o[d], pa[kc][0], pa[kc][1], pa[kc][2], pa[kc][3], b0r, b1r);
+        }
+    }
+    // the node partial of every head of the group: acc[128], m, l
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int h = g + half * 8;
+      if (h < G) {
+        float* np = npart + h * kPartStride;
+#pragma unroll
+        for (int d = 0; d < 16; ++d) {
+          np[d * 8 + 2 * c] = o[d][2 * half];
+          np[d * 8 + 2 * c + 1] = o[d][2 * half + 1];
+        }
+        if (c == 0) {
+          np[128] = half ? m1 : m0;
+          np[129] = half ? l1 : l0;
+        }
+      }
+    }
+  }
+
+  pdl_wait();  // the prefix chunk partials are complete
+  const int NP = p.sp ? p.sp->prompt_len : p.NP;
+  const int nchunks = prefix_nchunks(NP, p.H);
+  const int d0 = lane * 4;
+  uint16_t* out = static_cast<uint16_t*>(p.out) + static_cast<int64_t>(row) * p.som + d0;
+  if (row >= live) {  // padding row of a bucketed engine step: zeros, no reads
+    for (int h = 0; h < G; ++h)
+      *reinterpret_cast<uint2*>(out + (kvh * G + h) * p.soh) = make_uint2(0u, 0u);
+    return;
+  }
+  // The row's chunk partials (every head of the group) are copied into the
+  // staging area with all copies in flight; all of them when they fit (config 3:
+  // 5 chunks x 7 heads), else one head's chunks at a time.
+  constexpr int kPiece = kPartStride * 4;
+  float* pieces = reinterpret_cast<float*>(nsm);
+  const int cap_pieces = kStageBytes / kPiece;
+  const bool all_at_once = G * nchunks <= cap_pieces;
+  auto stage = [&](int h_first, int h_count) {   // pieces (chunk k, head h_first + j) at index j * nchunks + k
+    __syncwarp();
+    for (int t = lane; t < h_count * nchunks * (kPiece / 16); t += 32) {
+      const int pc = t % (kPiece / 16), pi = t / (kPiece / 16);
+      const int k = pi % nchunks, hh = h_first + pi / nchunks;
+      const float* src = part + ((static_cast<int64_t>(k) * p.H + kvh * G + hh) * p.M + row) * kPartStride;
+      cp_async16(reinterpret_cast<uint8_t*>(pieces) + pi * kPiece + pc * 16,
+                 reinterpret_cast<const uint8_t*>(src) + pc * 16, 16u);
+    }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    __syncwarp();
+  };
+  __syncwarp();   // the node partial written by the fold is visible to every lane
+  if (all_at_once && nchunks > 0) stage(0, G);
+  for (int h = 0; h < G; ++h) {
+    if (!all_at_once && nchunks > 0) stage(h, 1);
+    const float* ph = pieces + (all_at_once ? h * nchunks : 0) * kPartStride;
+    // prefix chunk partials in ascending chunk order, then the node partial
+    NodeAcc r{-INFINITY, 0.f, {0.f, 0.f, 0.f, 0.f}};
+    for (int k = 0; k < nchunks; ++k) {
+      const float* o = ph + k * kPartStride;
+      const float4 v = *reinterpret_cast<const float4*>(o + d0);
+      const float ca[4] = {v.x, v.y, v.z, v.w};
+      merge_into(r, o[128], o[129], ca);
+    }
+    const float* np = npart + h * kPartStride;
+    const float4 v = *reinterpret_cast<const float4*>(np + d0);
+    const float ca[4] = {v.x, v.y, v.z, v.w};
+    merge_into(r, np[128], np[129], ca);
+    uint16_t b[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) b[e] = f32_to_bf16_bits(__fdiv_rn(r.acc[e], r.l));
+    *reinterpret_cast<uint2*>(out + (kvh * G + h) * p.soh) =
+        make_uint2(static_cast<uint32_t>(b[0]) | (static_cast<uint32_t>(b[1]) << 16),
+                   static_cast<uint32_t>(b[2]) | (static_cast<uint32_t>(b[3]) << 16));
+  }
+}
 template <typename T, int R>
 static int launch_nodes_r(const AttnDev& p, const float* part, int grid, cudaStream_t stream, bool pdl) {
   const int G = p.H / p.HK;
@@ -477,6 +765,12 @@ static int launch_nodes(const AttnDev& p, const float* part, cudaStream_t stream
   if (G > kMaxGroup) return RB_ERR_UNSUPPORTED;
   const int items = p.M * p.HK;
   if (items <= 0) return RB_OK;
+  if (sizeof(T) == 2) {   // bf16: one warp per item on the tensor cores
+    const int dyn = nm::smem_bytes(G);
+    if (cudaFuncSetAttribute(attn_nodes_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) != cudaSuccess)
+      return RB_ERR_CUDA;
+    return launch_k(attn_nodes_mma, dim3(items), dim3(32), dyn, stream, pdl, p, part);
+  }
   return launch_nodes_r<T, 1>(p, part, items, stream, pdl);
 }
 
