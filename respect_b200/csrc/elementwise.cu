@@ -17,26 +17,36 @@ template <> struct IsBF16<uint16_t> { static constexpr bool value = true; };
 
 // ------------------------------------------------------------------ RMSNorm
 // One group of NT threads per row (respect/kernels/rmsnorm.py:12-22). Each
-// thread sums a fixed strided subset of the row, then a fixed warp tree and a
-// fixed cross-warp order: the row's bits never depend on the number of rows.
-// Rounding points follow PyTorch: upcast, mean of squares, rsqrt, downcast to
-// the input dtype, multiply by the weight, downcast.
-template <typename TX, typename TW, int NT>
+// thread sums a fixed subset of the row, then a fixed warp tree and a fixed
+// cross-warp order: the row's bits never depend on the number of rows.
+// Ownership: with VEC (NT = 1024, N % 4 == 0) thread t owns the 4-element
+// groups 4(t + j NT) .. +3, summed j-major; otherwise the elements t + j NT.
+// The engine's fused norms (embed / residual) use the same rule, so they stay
+// bitwise equal to this operator. Rounding points follow PyTorch: upcast, mean
+// of squares, rsqrt, downcast to the input dtype, multiply by the weight,
+// downcast.
+template <typename TX, typename TW, int NT, bool VEC>
 __global__ void __launch_bounds__(NT >= 256 ? NT : 256) rmsnorm_kernel(const TX* __restrict__ x,
                                                                       const TW* __restrict__ w,
                                                                       TX* __restrict__ y, int M, int N, float eps) {
   constexpr int kRowsPerBlock = NT >= 256 ? 1 : 256 / NT;  // blocks of max(NT, 256) threads
   constexpr int kWarps = NT / 32;
+  constexpr int kStep = VEC ? 4 * NT : NT;
+  constexpr int kLanes = VEC ? 4 : 1;
   __shared__ float red[kRowsPerBlock][kWarps];
   const int sub = threadIdx.x / NT, t = threadIdx.x % NT;
   const int row = blockIdx.x * kRowsPerBlock + sub;
   const bool live = row < M;
   const TX* xr = x + static_cast<int64_t>(live ? row : 0) * N;
+  const int first = VEC ? 4 * t : t;
   float ss = 0.f;
   if (live)
-    for (int i = t; i < N; i += NT) {
-      const float v = ld_f32(xr + i);
-      ss = fmaf(v, v, ss);
+    for (int i = first; i < N; i += kStep) {
+#pragma unroll
+      for (int c = 0; c < kLanes; ++c) {
+        const float v = ld_f32(xr + i + c);
+        ss = fmaf(v, v, ss);
+      }
     }
   ss = warp_sum(ss);
   ss = __shfl_sync(0xffffffffu, ss, 0);
@@ -62,12 +72,14 @@ static int rmsnorm_t(const void* x, const void* w, void* y, int M, int N, float 
   TX* yp = static_cast<TX*>(y);
   if (M <= 0) return RB_OK;
   // Threads per row depend on N only.
-  if (N >= 2048) {
-    rmsnorm_kernel<TX, TW, 1024><<<M, 1024, 0, s>>>(xp, wp, yp, M, N, eps);
+  if (N >= 2048 && N % 4 == 0) {
+    rmsnorm_kernel<TX, TW, 1024, true><<<M, 1024, 0, s>>>(xp, wp, yp, M, N, eps);
+  } else if (N >= 2048) {
+    rmsnorm_kernel<TX, TW, 1024, false><<<M, 1024, 0, s>>>(xp, wp, yp, M, N, eps);
   } else if (N >= 512) {
-    rmsnorm_kernel<TX, TW, 128><<<(M + 1) / 2, 256, 0, s>>>(xp, wp, yp, M, N, eps);
+    rmsnorm_kernel<TX, TW, 128, false><<<(M + 1) / 2, 256, 0, s>>>(xp, wp, yp, M, N, eps);
   } else {
-    rmsnorm_kernel<TX, TW, 32><<<(M + 7) / 8, 256, 0, s>>>(xp, wp, yp, M, N, eps);
+    rmsnorm_kernel<TX, TW, 32, false><<<(M + 7) / 8, 256, 0, s>>>(xp, wp, yp, M, N, eps);
   }
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;
 }

@@ -95,10 +95,13 @@ __global__ void __launch_bounds__(NT) embed_norm_kernel(const StepParams* __rest
     id = 0;
   }
   const uint16_t* er = emb + static_cast<int64_t>(id) * N;
+  // element k of this thread: NT = 1024 rows use the vector ownership of
+  // rmsnorm_kernel (4-column groups), narrower rows the strided one
+  auto elem = [](int k) { return NT == 1024 ? 4 * (threadIdx.x + (k >> 2) * NT) + (k & 3) : threadIdx.x + k * NT; };
   float v[EPT];
 #pragma unroll
   for (int k = 0; k < EPT; ++k) {
-    const int i = threadIdx.x + k * NT;
+    const int i = elem(k);
     v[k] = 0.f;
     if (i < N) {
       const uint16_t b = er[i];
@@ -109,7 +112,7 @@ __global__ void __launch_bounds__(NT) embed_norm_kernel(const StepParams* __rest
   const float r = row_inv_rms<NT>(v, EPT, N, eps, red);
 #pragma unroll
   for (int k = 0; k < EPT; ++k) {
-    const int i = threadIdx.x + k * NT;
+    const int i = elem(k);
     if (i < N) {
       const float xh = round_bf16(v[k] * r);
       xn[static_cast<int64_t>(row) * N + i] = f32_to_bf16_bits(bf16_bits_to_f32(w[i]) * xh);
@@ -176,6 +179,80 @@ __global__ void __maxnreg__(40) resid_norm_kernel(const StepParams* __restrict__
     if (i < N) {
       const float xh = round_bf16(v[k] * r);
       xn[static_cast<int64_t>(row) * N + i] = f32_to_bf16_bits(bf16_bits_to_f32(wv[k]) * xh);
+    }
+  }
+}
+
+// resid_norm_kernel for NT = 1024 rows in the vector ownership of
+// rmsnorm_kernel: thread t owns the 4-column groups 4(t + j NT) .. +3
+// (j < G4). A group's split partials are read as float4, kSplitBatch splits
+// in flight at once (one round of loads for up to kSplitBatch splits) and
+// added in ascending split order, as in the scalar kernel; h and xn move as
+// 8-byte groups. Same 40-register cap, for the same co-residency reason.
+constexpr int kSplitBatch = 5;
+template <int G4>
+__global__ void __maxnreg__(40) resid_norm_vec_kernel(const StepParams* __restrict__ sp, const float* __restrict__ part,
+                                                      int splits, int M, uint16_t* __restrict__ h,
+                                                      const uint16_t* __restrict__ w, uint16_t* __restrict__ xn, int N,
+                                                      float eps) {
+  constexpr int NT = 1024;
+  __shared__ float red[NT / 32];
+  const int row = blockIdx.x;
+  pdl_trigger();
+  uint16_t wv[4 * G4];  // the norm weights never change: read before waiting for the GEMM
+#pragma unroll
+  for (int j = 0; j < G4; ++j) {
+    const int i = 4 * (threadIdx.x + j * NT);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) wv[4 * j + c] = i < N ? w[i + c] : 0;
+  }
+  pdl_wait();
+  if (row >= sp->q) return;
+  const int64_t plane = static_cast<int64_t>(M) * N;
+  float v[4 * G4];
+#pragma unroll
+  for (int j = 0; j < G4; ++j) {
+    const int i = 4 * (threadIdx.x + j * NT);
+    const bool live = i < N;
+    const float4* p = reinterpret_cast<const float4*>(part + static_cast<int64_t>(row) * N + i);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < splits; s0 += kSplitBatch) {
+      float4 t[kSplitBatch];
+#pragma unroll
+      for (int b = 0; b < kSplitBatch; ++b)
+        t[b] = (live && s0 + b < splits) ? __ldcg(p + (s0 + b) * (plane / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int b = 0; b < kSplitBatch; ++b) {
+        if (s0 + b >= splits) break;
+        if (s0 + b == 0) {
+          acc = t[0];
+        } else {
+          acc.x += t[b].x; acc.y += t[b].y; acc.z += t[b].z; acc.w += t[b].w;
+        }
+      }
+    }
+    v[4 * j] = v[4 * j + 1] = v[4 * j + 2] = v[4 * j + 3] = 0.f;
+    if (live) {
+      uint2* hp = reinterpret_cast<uint2*>(h + static_cast<int64_t>(row) * N + i);
+      const uint2 hb = *hp;
+      const float a[4] = {acc.x, acc.y, acc.z, acc.w};
+      const uint32_t hw[4] = {hb.x & 0xffffu, hb.x >> 16, hb.y & 0xffffu, hb.y >> 16};
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        v[4 * j + c] = round_bf16(bf16_bits_to_f32(static_cast<uint16_t>(hw[c])) + round_bf16(a[c]));
+      *hp = make_uint2(pack_bf16x2(v[4 * j], v[4 * j + 1]), pack_bf16x2(v[4 * j + 2], v[4 * j + 3]));
+    }
+  }
+  const float r = row_inv_rms<NT>(v, 4 * G4, N, eps, red);
+#pragma unroll
+  for (int j = 0; j < G4; ++j) {
+    const int i = 4 * (threadIdx.x + j * NT);
+    if (i < N) {
+      float y[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) y[c] = bf16_bits_to_f32(wv[4 * j + c]) * round_bf16(v[4 * j + c] * r);
+      *reinterpret_cast<uint2*>(xn + static_cast<int64_t>(row) * N + i) =
+          make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
     }
   }
 }
@@ -517,6 +594,12 @@ int launch_resid_norm(rb_engine* e, int splits, int rows, const void* w, cudaStr
   const rb_model_config& c = e->cfg;
   return launch_norm_nt(c.hidden, [&](auto nt, auto ept) {
     constexpr int NT = decltype(nt)::value, EPT = decltype(ept)::value;
+    if constexpr (NT == 1024) {
+      constexpr int G4 = EPT < 4 ? 1 : EPT / 4;
+      return launch_k(resid_norm_vec_kernel<G4>, dim3(rows), dim3(NT), 0, st, true,
+                      static_cast<const StepParams*>(e->d_params), static_cast<const float*>(e->part), splits, rows,
+                      e->h, static_cast<const uint16_t*>(w), e->xn, c.hidden, c.rms_eps);
+    }
     auto go = [&](auto ms) {
       constexpr int MAXS = decltype(ms)::value;
       return launch_k(resid_norm_kernel<NT, EPT, MAXS>, dim3(rows), dim3(NT), 0, st, true,
@@ -546,7 +629,8 @@ int enqueue_step(rb_engine* e, int rows, cudaStream_t st) {
 
   RB_TRY(launch_norm_nt(hid, [&](auto nt, auto ept) {
     constexpr int NT = decltype(nt)::value, EPT = decltype(ept)::value;
-    return launch_k(embed_norm_kernel<NT, EPT>, dim3(rows), dim3(NT), 0, st, true,
+    constexpr int EV = NT == 1024 && EPT < 4 ? 4 : EPT;  // whole 4-column groups per thread
+    return launch_k(embed_norm_kernel<NT, EV>, dim3(rows), dim3(NT), 0, st, true,
                     static_cast<const StepParams*>(e->d_params), static_cast<const int32_t*>(e->d_ids),
                     static_cast<const uint16_t*>(e->w.embed), static_cast<const uint16_t*>(e->layers[0].in_norm),
                     e->h, e->xn, hid, c.vocab, c.rms_eps, static_cast<const int32_t*>(e->d_parents),
