@@ -477,7 +477,8 @@ constexpr int kQRows = 16, kListRows = 32;
 constexpr int kQBytes = kQRows * kPitch * 2;      // 4352
 constexpr int kKVBytes = kListRows * kPitch * 2;  // 8704 each for K and V
 constexpr int kStageBytes = kQBytes + 2 * kKVBytes;
-__host__ __device__ inline int smem_bytes(int G) { return kStageBytes + G * kPartStride * 4 + kListRows * 4; }
+// staging | node partials [G][kPartStride] | list slots [kListRows] | mbarrier of the merge's bulk copies
+__host__ __device__ inline int smem_bytes(int G) { return kStageBytes + G * kPartStride * 4 + kListRows * 4 + 16; }
 }  // namespace nm
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -512,7 +513,12 @@ __global__ void __launch_bounds__(32) attn_nodes_mma(const AttnDev p, const floa
   const int lane = threadIdx.x, g = lane >> 2, c = lane & 3;
   const int live = p.sp ? p.sp->q : p.M;
   const int row = blockIdx.x % p.M, kvh = blockIdx.x / p.M;
+  const uint32_t sbar = smem_u32(nsm + kStageBytes + G * kPartStride * 4 + kListRows * 4);
   pdl_trigger();
+  if (lane == 0) {
+    mbar_init(sbar, 1);
+    fence_mbar_init();
+  }
   for (int h = lane; h < G; h += 32) npart[h * kPartStride + 128] = -INFINITY;   // empty node partial
 
   if (row < live) {
@@ -708,22 +714,30 @@ __global__ void __launch_bounds__(32) attn_nodes_mma(const AttnDev p, const floa
   float* pieces = reinterpret_cast<float*>(nsm);
   const int cap_pieces = kStageBytes / kPiece;
   const bool all_at_once = G * nchunks <= cap_pieces;
+  // One bulk copy per piece (the TMA engine moves each 528-byte piece), all
+  // completing on one mbarrier: a single round trip instead of a lane-by-lane
+  // stream of 16-byte copies.
+  uint32_t sphase = 0;
   auto stage = [&](int h_first, int h_count) {   // pieces (chunk k, head h_first + j) at index j * nchunks + k
+    fence_proxy_async_smem();   // this lane's generic reads of the staging area come before the copies' writes
     __syncwarp();
-    for (int t = lane; t < h_count * nchunks * (kPiece / 16); t += 32) {
-      const int pc = t % (kPiece / 16), pi = t / (kPiece / 16);
+    const int n = h_count * nchunks;
+    if (lane == 0) mbar_arrive_expect_tx(sbar, static_cast<uint32_t>(n * kPiece));
+    __syncwarp();
+    for (int pi = lane; pi < n; pi += 32) {
       const int k = pi % nchunks, hh = h_first + pi / nchunks;
       const float* src = part + ((static_cast<int64_t>(k) * p.H + kvh * G + hh) * p.M + row) * kPartStride;
-      cp_async16(reinterpret_cast<uint8_t*>(pieces) + pi * kPiece + pc * 16,
-                 reinterpret_cast<const uint8_t*>(src) + pc * 16, 16u);
+      bulk_load(smem_u32(reinterpret_cast<uint8_t*>(pieces) + pi * kPiece), src, kPiece, sbar);
     }
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    const bool ok = mbar_wait(sbar, sphase, 0x231);
+    sphase ^= 1u;
     __syncwarp();
+    return ok;
   };
   __syncwarp();   // the node partial written by the fold is visible to every lane
-  if (all_at_once && nchunks > 0) stage(0, G);
+  if (all_at_once && nchunks > 0 && !stage(0, G)) return;
   for (int h = 0; h < G; ++h) {
-    if (!all_at_once && nchunks > 0) stage(h, 1);
+    if (!all_at_once && nchunks > 0 && !stage(h, 1)) return;
     const float* ph = pieces + (all_at_once ? h * nchunks : 0) * kPartStride;
     // prefix chunk partials in ascending chunk order, then the node partial
     NodeAcc r{-INFINITY, 0.f, {0.f, 0.f, 0.f, 0.f}};
@@ -825,6 +839,7 @@ int attn_launch(const rb_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t s
   if (a->M == 0) return RB_OK;
   const size_t need = attn_workspace_bytes(a->H, a->M, a->D, a->NP);
   if (!ws || ws_bytes < need) return RB_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(ws) & 15) return RB_ERR_UNSUPPORTED;  // partials move by bulk copies
   AttnDev p{};
   p.H = a->H; p.M = a->M; p.HK = a->HK; p.NP = a->NP; p.NN = a->NN;
   p.q = a->q; p.sqh = a->sqh; p.sqm = a->sqm;

@@ -152,6 +152,13 @@ __device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t byt
                "r"(src), "r"(bytes)
                : "memory");
 }
+// Plain (untiled) bulk copy global -> shared::cta (no multicast) completing on
+// `bar` with complete_tx; both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Every committed bulk store has finished reading its shared-memory source (the
 // buffer may be reused and the CTA may exit; the global writes are performed by
