@@ -660,15 +660,20 @@ __global__ void __launch_bounds__(32) attn_nodes_mma(const AttnDev p, const floa
         o[d][0] *= al0; o[d][1] *= al0;
         o[d][2] *= al1; o[d][3] *= al1;
       }
-      // 5. O += bf16(P) V over the 32 entries (two 16-entry k-steps)
-      uint32_t pa[2][4];
+      // 5. O += P V over the 32 entries (two 16-entry k-steps). The node keys'
+      // weights stay fp32 in the reference (attention.py:59-66, p * v in fp32),
+      // so P goes in as two bf16 parts, hi = bf16(p) and lo = bf16(p - hi)
+      // (p to about 16 significant bits), each times the bf16 V rows.
+      uint32_t pa[2][4], pl[2][4];
 #pragma unroll
-      for (int kc = 0; kc < 2; ++kc) {
-        pa[kc][0] = pack_bf16x2(sc[2 * kc][0], sc[2 * kc][1]);
-        pa[kc][1] = pack_bf16x2(sc[2 * kc][2], sc[2 * kc][3]);
-        pa[kc][2] = pack_bf16x2(sc[2 * kc + 1][0], sc[2 * kc + 1][1]);
-        pa[kc][3] = pack_bf16x2(sc[2 * kc + 1][2], sc[2 * kc + 1][3]);
-      }
+      for (int kc = 0; kc < 2; ++kc)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int j = 2 * kc + (i >> 1), e = (i & 1) * 2;   // pieces: (j, e), (j, e + 1)
+          const float h0 = round_bf16(sc[j][e]), h1 = round_bf16(sc[j][e + 1]);
+          pa[kc][i] = pack_bf16x2(h0, h1);
+          pl[kc][i] = pack_bf16x2(sc[j][e] - h0, sc[j][e + 1] - h1);
+        }
 #pragma unroll
       for (int d = 0; d < 16; ++d)
 #pragma unroll
@@ -676,6 +681,7 @@ __global__ void __launch_bounds__(32) attn_nodes_mma(const AttnDev p, const floa
           uint32_t b0r, b1r;
           ldsm_x2_t(sV + ((kc * 16 + (lane & 15)) * kPitch + d * 8) * 2, b0r, b1r);
           mma_bf16_16816(o[d], pa[kc][0], pa[kc][1], pa[kc][2], pa[kc][3], b0r, b1r);
+          mma_bf16_16816(o[d], pl[kc][0], pl[kc][1], pl[kc][2], pl[kc][3], b0r, b1r);
         }
     }
     // the node partial of every head of the group: acc[128], m, l
