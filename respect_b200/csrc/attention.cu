@@ -757,9 +757,12 @@ __global__ void __launch_bounds__(32) attn_nodes_mma(const AttnDev p, const floa
     const float4 v = *reinterpret_cast<const float4*>(np + d0);
     const float ca[4] = {v.x, v.y, v.z, v.w};
     merge_into(r, np[128], np[129], ca);
+    // bf16 output: one correctly rounded reciprocal per head, then products (the
+    // reference divides with Triton's fp32 `/`, itself not correctly rounded)
+    const float rl = __frcp_rn(r.l);
     uint16_t b[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) b[e] = f32_to_bf16_bits(__fdiv_rn(r.acc[e], r.l));
+    for (int e = 0; e < 4; ++e) b[e] = f32_to_bf16_bits(r.acc[e] * rl);
     *reinterpret_cast<uint2*>(out + (kvh * G + h) * p.soh) =
         make_uint2(static_cast<uint32_t>(b[0]) | (static_cast<uint32_t>(b[1]) << 16),
                    static_cast<uint32_t>(b[2]) | (static_cast<uint32_t>(b[3]) << 16));
