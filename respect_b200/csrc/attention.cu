@@ -37,31 +37,88 @@ template <> __device__ __forceinline__ void ld4<uint16_t>(const uint16_t* p, flo
   v[3] = bf16_bits_to_f32(static_cast<uint16_t>(t.y >> 16));
 }
 
-// ----------------------------------------------------------------- prefix (SIMT)
-// fp32 data. Block = 4 warps = 16 query rows of one head over one prefix
-// chunk. Key tiles of 32 keys are copied into shared memory with cp.async, two
-// buffers deep (tile t+1 lands while tile t is computed); lane j scores key j
-// of the tile.
-constexpr int kSimtTK = 32, kSimtRB = 16, kSimtKPitch = 128 + 4;  // K rows: 16-byte aligned, float4 reads conflict-free
-constexpr int kSimtSmem = (2 * kSimtTK * kSimtKPitch + 2 * kSimtTK * 128 + kSimtRB * 128) * 4;
-
+// ----------------------------------------------------------------- cp.async
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
   // src_bytes = 0 copies nothing and zero-fills the 16 bytes
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
                : "memory");
 }
 
-template <typename T>
-__global__ void __launch_bounds__(128) attn_prefix_simt(const AttnDev p, float* __restrict__ part, int nchunks) {
-  static_assert(sizeof(T) == 4, "the CUDA-core prefix serves fp32 data (bf16 runs on the tensor cores)");
-  constexpr int D = 128, TK = kSimtTK, RB = kSimtRB;
-  extern __shared__ __align__(16) float simt_smem[];
-  auto ks = reinterpret_cast<float(*)[TK][kSimtKPitch]>(simt_smem);              // [2][TK][pitch]
-  auto vs = reinterpret_cast<float(*)[TK][D]>(simt_smem + 2 * TK * kSimtKPitch);  // [2][TK][D]
-  auto qs = reinterpret_cast<float(*)[D]>(simt_smem + 2 * TK * kSimtKPitch + 2 * TK * D);
-  const int c = blockIdx.x, h = blockIdx.y, r0 = blockIdx.z * RB;
+// ----------------------------------------------------------------- prefix (fp32 data, tensor cores)
+// fp32 data on the tensor cores. Each score and each P·V term is the sum of
+// three tf32 products, hi·hi + hi·lo + lo·hi (q: hi = tf32(x) rounded to
+// nearest, ties away, lo = tf32(x - hi); K, V and P: hi = x truncated to tf32,
+// lo = x - hi): at most about 2^-19 relative error per term, fp32 accumulation
+// (mma.sync.m16n8k8 tf32, independent of the row count).
+//
+// Block = 4 warps = 16 query rows of one head over one prefix chunk. Key tiles
+// of 32 keys are copied into shared memory with cp.async (K two tiles deep: the
+// next tile's K lands during this tile; V one deep: it lands during the S
+// products of its tile); warp w takes keys
+// 8w .. 8w + 7 of every tile (one n-tile of S, one k-step of P·V) and keeps its
+// own online-softmax state, so no warp waits for another within a tile. At the
+// end the four states are merged in warp order into the chunk partial.
+//
+// Fragment layouts (lane = 4g + t): the 128 head dims enter the S products in a
+// fixed permuted order, k-step 2i + o (o = 0, 1) position t <- dim 16i + 4t + 2o
+// and position t + 4 <- dim 16i + 4t + 2o + 1, so that a lane's A (q) and B (k)
+// values of two k-steps are one float4. The P·V k-step takes the warp's 8 keys in
+// the order (0, 2, 4, 6 | 1, 3, 5, 7), which makes S's accumulator fragment the P
+// A-fragment as it stands; P·V n-tile j, position n <- dim 32(j / 4) + 4n + j % 4,
+// so a lane's V values of four n-tiles are one float4.
+namespace t32 {
+constexpr int kRows = 16, kTK = 32, kD = 128;
+constexpr int kQP = 144, kKP = 144, kVP = 132;   // shared-memory row pitches (floats): conflict-free fragment reads
+constexpr int kQFloats = kRows * kQP;            // one of Q hi / Q lo
+constexpr int kKFloats = kTK * kKP, kVFloats = kTK * kVP;
+constexpr int kMergeFloats = 4 * kRows * kPartStride;   // the four warps' states (reuses the K area)
+static_assert(kMergeFloats <= 2 * kKFloats, "merge area fits in the K tiles");
+constexpr int kSmemBytes = (2 * kQFloats + 2 * kKFloats + kVFloats) * 4;
+}  // namespace t32
+
+__device__ __forceinline__ uint32_t tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+// d (16x8 fp32) += a (16x8 tf32, row-major) * b (8x8 tf32, column-major)
+__device__ __forceinline__ void mma_tf32_1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// d += (ah + al)(bh + bl) without the al·bl term
+__device__ __forceinline__ void mma_3xtf32(float (&d)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
+                                           uint32_t bh0, uint32_t bh1, uint32_t bl0, uint32_t bl1) {
+  mma_tf32_1688(d, ah[0], ah[1], ah[2], ah[3], bh0, bh1);
+  mma_tf32_1688(d, ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+  mma_tf32_1688(d, al[0], al[1], al[2], al[3], bh0, bh1);
+}
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = tf32_rna(x);
+  lo = tf32_rna(x - __uint_as_float(hi));
+}
+// The per-tile split of K, V and P on the integer and FMA pipes (the conversion
+// above runs on the slower multi-function pipe): hi = x with the 13 low mantissa
+// bits cleared, lo = x - hi (exact), whose own low bits the tf32 MMA drops:
+// |x - hi - lo_tf32| < 2^-20 |x|.
+__device__ __forceinline__ void split_tf32_fast(float x, uint32_t& hi, uint32_t& lo) {
+  hi = __float_as_uint(x) & 0xFFFFE000u;
+  lo = __float_as_uint(x - __uint_as_float(hi));
+}
+
+__global__ void __launch_bounds__(128) attn_prefix_tf32(const AttnDev p, float* __restrict__ part) {
+  using namespace t32;
+  extern __shared__ __align__(16) float t32_smem[];
+  uint32_t* qh = reinterpret_cast<uint32_t*>(t32_smem);          // [16][kQP] tf32 hi of q
+  uint32_t* ql = qh + kQFloats;                                  // [16][kQP] tf32 lo of q
+  float* ks0 = t32_smem + 2 * kQFloats;                          // [2][32][kKP]
+  float* vs = ks0 + 2 * kKFloats;                                // [32][kVP]
+  const int c = blockIdx.x, h = blockIdx.y, r0 = blockIdx.z * kRows;
   const int kvh = h / (p.H / p.HK);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   pdl_trigger();
   pdl_wait();
   const int NP = p.sp ? p.sp->prompt_len : p.NP;
@@ -70,108 +127,190 @@ __global__ void __launch_bounds__(128) attn_prefix_simt(const AttnDev p, float* 
   const int k0 = c * C;
   const int k1 = min(NP, k0 + C);
   if (k0 >= k1 || r0 >= M) return;  // chunk beyond the prefix / rows beyond the live ones
-  const T* q = static_cast<const T*>(p.q);
-  const T* kp = static_cast<const T*>(p.kp);
-  const T* vp = static_cast<const T*>(p.vp);
-  // Tile starting at key kt into buffer b; keys past the chunk end are zero-filled.
-  auto stage = [&](int b, int kt) {
-    for (int i = threadIdx.x; i < TK * D / 4; i += blockDim.x) {
-      const int j = i / (D / 4), d4 = (i % (D / 4)) * 4;
-      const bool ok = kt + j < k1;
-      const int key = ok ? kt + j : k0;
-      cp_async16(&ks[b][j][d4], kp + kvh * p.skph + static_cast<int64_t>(key) * p.skpn + d4, ok ? 16u : 0u);
-      cp_async16(&vs[b][j][d4], vp + kvh * p.svph + static_cast<int64_t>(key) * p.svpn + d4, ok ? 16u : 0u);
+  const float* q = static_cast<const float*>(p.q);
+  const float* kp = static_cast<const float*>(p.kp);
+  const float* vp = static_cast<const float*>(p.vp);
+  for (int i = threadIdx.x; i < kRows * kD; i += blockDim.x) {
+    const int r = i / kD, d = i % kD;
+    const float x = (r0 + r < M) ? q[h * p.sqh + static_cast<int64_t>(r0 + r) * p.sqm + d] : 0.f;
+    uint32_t hi, lo;
+    split_tf32(x, hi, lo);
+    qh[r * kQP + d] = hi;
+    ql[r * kQP + d] = lo;
+  }
+  const float scale2 = p.sm_scale * kLog2e;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;   // rows g and g + 8
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[j][e] = 0.f;
+  // K or V rows of the tile at key kt (keys past the chunk end zero-filled), one cp.async group
+  // (thread = row j0 + 4 it, 16 bytes at dim 4 lane: one row per warp per step)
+  auto load_rows = [&](float* dst, int pitch, const float* src, int64_t sh, int64_t sn, int kt) {
+    const int j0 = threadIdx.x >> 5;
+    const float* s0 = src + kvh * sh + static_cast<int64_t>(kt + j0) * sn + 4 * lane;
+    const float* sf = src + kvh * sh + static_cast<int64_t>(k0) * sn + 4 * lane;   // any valid row (zero-filled)
+    float* d0 = dst + j0 * pitch + 4 * lane;
+    const int64_t step = 4 * sn;
+#pragma unroll
+    for (int it = 0; it < kTK / 4; ++it) {
+      const bool ok = kt + j0 + 4 * it < k1;
+      cp_async16(d0 + it * 4 * pitch, ok ? s0 + it * step : sf, ok ? 16u : 0u);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  stage(0, k0);
-
-  for (int i = threadIdx.x; i < RB * D; i += blockDim.x) {
-    const int r = i / D, d = i % D;
-    qs[r][d] = (r0 + r < M) ? ldf(q + h * p.sqh + static_cast<int64_t>(r0 + r) * p.sqm + d) : 0.f;
-  }
-  float m[4], l[4], acc[4][4];
+  load_rows(ks0, kKP, kp, p.skph, p.skpn, k0);
+  load_rows(vs, kVP, vp, p.svph, p.svpn, k0);
+  for (int kt = k0, tile = 0; kt < k1; kt += kTK, ++tile) {
+    const float* ks = ks0 + (tile & 1) * kKFloats;
+    // the next tile's K (its buffer was last read by the previous tile's S products)
+    if (kt + kTK < k1) load_rows(ks0 + ((tile + 1) & 1) * kKFloats, kKP, kp, p.skph, p.skpn, kt + kTK);
+    else asm volatile("cp.async.commit_group;" ::: "memory");   // an empty group keeps the counts below
+    asm volatile("cp.async.wait_group 2;" ::: "memory");        // this tile's K (V and the next K may pend)
+    __syncthreads();   // this tile's K (and q) visible to every warp
+    const int kw = kt + warp * 8;   // the warp's first key
+    const bool act = kw < k1;       // uniform per warp
+    uint32_t ph[4], pl[4];          // P of the warp's keys, tf32 hi / lo
+    if (act) {
+      // S (16 rows x the warp's 8 keys). Six independent accumulators (hi·hi,
+      // hi·lo, lo·hi, each for even and odd k-steps) keep the MMA chains short;
+      // they are added in a fixed order at the end.
+      float acc[6][4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    m[i] = -INFINITY; l[i] = 0.f;
+      for (int a = 0; a < 6; ++a)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
-  }
-  const float scale2 = p.sm_scale * kLog2e;
-  for (int kt = k0, tile = 0; kt < k1; kt += TK, ++tile) {
-    const int b = tile & 1;
-    if (kt + TK < k1) {
-      stage(b ^ 1, kt + TK);  // its buffer was last read by the previous tile, which every warp has finished
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
+        for (int e = 0; e < 4; ++e) acc[a][e] = 0.f;
+      const float* kr = ks + (warp * 8 + g) * kKP + 4 * t;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint4 a_g = *reinterpret_cast<const uint4*>(qh + g * kQP + 16 * i + 4 * t);
+        const uint4 a_g8 = *reinterpret_cast<const uint4*>(qh + (g + 8) * kQP + 16 * i + 4 * t);
+        const uint4 b_g = *reinterpret_cast<const uint4*>(ql + g * kQP + 16 * i + 4 * t);
+        const uint4 b_g8 = *reinterpret_cast<const uint4*>(ql + (g + 8) * kQP + 16 * i + 4 * t);
+        const float4 kv = *reinterpret_cast<const float4*>(kr + 16 * i);
+        uint32_t kh[4], kl[4];
+        split_tf32_fast(kv.x, kh[0], kl[0]);
+        split_tf32_fast(kv.y, kh[1], kl[1]);
+        split_tf32_fast(kv.z, kh[2], kl[2]);
+        split_tf32_fast(kv.w, kh[3], kl[3]);
+        // k-step 2i: dims 16i + 4t + {0, 1}; k-step 2i + 1: dims 16i + 4t + {2, 3}
+        mma_tf32_1688(acc[0], a_g.x, a_g8.x, a_g.y, a_g8.y, kh[0], kh[1]);
+        mma_tf32_1688(acc[1], a_g.z, a_g8.z, a_g.w, a_g8.w, kh[2], kh[3]);
+        mma_tf32_1688(acc[2], a_g.x, a_g8.x, a_g.y, a_g8.y, kl[0], kl[1]);
+        mma_tf32_1688(acc[3], a_g.z, a_g8.z, a_g.w, a_g8.w, kl[2], kl[3]);
+        mma_tf32_1688(acc[4], b_g.x, b_g8.x, b_g.y, b_g8.y, kh[0], kh[1]);
+        mma_tf32_1688(acc[5], b_g.z, b_g8.z, b_g.w, b_g8.w, kh[2], kh[3]);
+      }
+      float s[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[e] = (acc[0][e] + acc[1][e]) + ((acc[2][e] + acc[3][e]) + (acc[4][e] + acc[5][e]));
+      // online softmax over the 8 keys (rows g: s[0], s[1]; rows g + 8: s[2], s[3])
+      const bool v0 = kw + 2 * t < k1, v1 = kw + 2 * t + 1 < k1;
+      s[0] = v0 ? s[0] * scale2 : -INFINITY;
+      s[1] = v1 ? s[1] * scale2 : -INFINITY;
+      s[2] = v0 ? s[2] * scale2 : -INFINITY;
+      s[3] = v1 ? s[3] * scale2 : -INFINITY;
+      float x0 = fmaxf(s[0], s[1]), x1 = fmaxf(s[2], s[3]);
+      x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, 1));
+      x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, 2));
+      x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, 1));
+      x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, 2));
+      const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);   // finite: the warp's first key is valid
+      const float al0 = fast_exp2(m0 - n0), al1 = fast_exp2(m1 - n1);
+      const float p0 = fast_exp2(s[0] - n0), p1 = fast_exp2(s[1] - n0);
+      const float p2 = fast_exp2(s[2] - n1), p3 = fast_exp2(s[3] - n1);
+      float rs0 = p0 + p1, rs1 = p2 + p3;
+      rs0 += __shfl_xor_sync(0xffffffffu, rs0, 1);
+      rs0 += __shfl_xor_sync(0xffffffffu, rs0, 2);
+      rs1 += __shfl_xor_sync(0xffffffffu, rs1, 1);
+      rs1 += __shfl_xor_sync(0xffffffffu, rs1, 2);
+      l0 = fmaf(l0, al0, rs0);
+      l1 = fmaf(l1, al1, rs1);
+      m0 = n0;
+      m1 = n1;
+      if (!__all_sync(0xffffffffu, al0 == 1.f && al1 == 1.f)) {   // the warp's running maxima moved
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          o[j][0] *= al0; o[j][1] *= al0;
+          o[j][2] *= al1; o[j][3] *= al1;
+        }
+      }
+      // A of P V = P in key order (2t, 2t + 1) -> positions (t, t + 4)
+      split_tf32_fast(p0, ph[0], pl[0]);   // (g, key 2t)
+      split_tf32_fast(p2, ph[1], pl[1]);   // (g + 8, key 2t)
+      split_tf32_fast(p1, ph[2], pl[2]);   // (g, key 2t + 1)
+      split_tf32_fast(p3, ph[3], pl[3]);   // (g + 8, key 2t + 1)
     }
-    __syncthreads();  // this tile (and q) visible to every warp
-    const bool kvalid = kt + lane < k1;
-    // Scores of the warp's four rows for key `lane`, in one pass over the dims:
-    // each float4 of the key row feeds the four rows (q rows are broadcast reads).
-    // Per row: four partial sums over d = 4k + e (fixed order), added pairwise.
-    float s4[4][4];
+    asm volatile("cp.async.wait_group 1;" ::: "memory");   // this tile's V (the next K may pend)
+    __syncthreads();   // this tile's V visible to every warp
+    if (act) {   // O += P V
+      const float* v0r = vs + (warp * 8 + 2 * t) * kVP + 4 * g;
+      const float* v1r = v0r + kVP;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+      for (int jq = 0; jq < 4; ++jq) {
+        const float4 va = *reinterpret_cast<const float4*>(v0r + 32 * jq);
+        const float4 vb = *reinterpret_cast<const float4*>(v1r + 32 * jq);
+        const float a4[4] = {va.x, va.y, va.z, va.w}, b4[4] = {vb.x, vb.y, vb.z, vb.w};
 #pragma unroll
-      for (int e = 0; e < 4; ++e) s4[i][e] = 0.f;
-#pragma unroll 4
-    for (int d = 0; d < D; d += 4) {
-      const float4 k4 = *reinterpret_cast<const float4*>(&ks[b][lane][d]);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 q4 = *reinterpret_cast<const float4*>(&qs[warp * 4 + i][d]);
-        s4[i][0] = fmaf(q4.x, k4.x, s4[i][0]);
-        s4[i][1] = fmaf(q4.y, k4.y, s4[i][1]);
-        s4[i][2] = fmaf(q4.z, k4.z, s4[i][2]);
-        s4[i][3] = fmaf(q4.w, k4.w, s4[i][3]);
+        for (int jr = 0; jr < 4; ++jr) {
+          uint32_t h0, l0b, h1, l1b;
+          split_tf32_fast(a4[jr], h0, l0b);
+          split_tf32_fast(b4[jr], h1, l1b);
+          mma_3xtf32(o[jq * 4 + jr], ph, pl, h0, h1, l0b, l1b);
+        }
       }
     }
-    float pv[4], alpha[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float s = (s4[i][0] + s4[i][1]) + (s4[i][2] + s4[i][3]);
-      s = kvalid ? s * scale2 : -INFINITY;
-      const float tmax = warp_max(s);
-      const float m_new = fmaxf(m[i], tmax);
-      alpha[i] = fast_exp2(m[i] - m_new);
-      const float pj = fast_exp2(s - m_new);
-      float psum = warp_sum(pj);
-      psum = __shfl_sync(0xffffffffu, psum, 0);
-      pv[i] = pj;
-      l[i] = fmaf(l[i], alpha[i], psum);
-      m[i] = m_new;
-    }
-    // P V of the four rows; each value row (this lane's four dims) is read once.
-    float t[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) t[i][e] = 0.f;
-#pragma unroll 4
-    for (int j = 0; j < TK; ++j) {
-      const float4 v4 = *reinterpret_cast<const float4*>(&vs[b][j][lane * 4]);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float pb = __shfl_sync(0xffffffffu, pv[i], j);
-        t[i][0] = fmaf(pb, v4.x, t[i][0]); t[i][1] = fmaf(pb, v4.y, t[i][1]);
-        t[i][2] = fmaf(pb, v4.z, t[i][2]); t[i][3] = fmaf(pb, v4.w, t[i][3]);
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[i][e] = fmaf(acc[i][e], alpha[i], t[i][e]);
-    __syncthreads();  // every warp is done with buffer b before the tile after next is copied into it
+    __syncthreads();   // every warp is done with this tile's V (and K) before they are overwritten
+    if (kt + kTK < k1) load_rows(vs, kVP, vp, p.svph, p.svpn, kt + kTK);
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");   // nothing in flight into the merge area
+  // merge the four warps' states in warp order: O = sum_w O_w 2^(m_w - m), l likewise
+  float* st = ks0;   // [4][16][kPartStride]: O at dims 0..127, m at 128, l at 129
+  float* mine = st + warp * kRows * kPartStride;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = r0 + warp * 4 + i;
-    if (r >= M) continue;
-    float* o = part + ((static_cast<int64_t>(c) * p.H + h) * p.M + r) * kPartStride;
-    *reinterpret_cast<float4*>(o + lane * 4) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-    if (lane == 0) { o[D] = m[i]; o[D + 1] = l[i]; }
+  for (int j = 0; j < 16; ++j) {
+    const int d = 32 * (j >> 2) + 8 * t + (j & 3);
+    mine[g * kPartStride + d] = o[j][0];
+    mine[g * kPartStride + d + 4] = o[j][1];
+    mine[(g + 8) * kPartStride + d] = o[j][2];
+    mine[(g + 8) * kPartStride + d + 4] = o[j][3];
+  }
+  if (t == 0) {
+    mine[g * kPartStride + 128] = m0;
+    mine[g * kPartStride + 129] = l0;
+    mine[(g + 8) * kPartStride + 128] = m1;
+    mine[(g + 8) * kPartStride + 129] = l1;
+  }
+  __syncthreads();
+  // thread (row r, dims 16 q .. 16 q + 15)
+  const int r = threadIdx.x >> 3, d0 = (threadIdx.x & 7) * 16;
+  if (r0 + r >= M) return;
+  float mw[4], mx = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    mw[w] = st[(w * kRows + r) * kPartStride + 128];
+    mx = fmaxf(mx, mw[w]);
+  }
+  float acc[16], lsum = 0.f;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    if (mw[w] == -INFINITY) continue;   // a warp without keys in this chunk
+    const float a = fast_exp2(mw[w] - mx);
+    const float* src = st + (w * kRows + r) * kPartStride;
+    lsum = fmaf(src[129], a, lsum);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) acc[e] = fmaf(src[d0 + e], a, acc[e]);
+  }
+  float* dst = part + ((static_cast<int64_t>(c) * p.H + h) * p.M + r0 + r) * kPartStride;
+#pragma unroll
+  for (int e = 0; e < 16; e += 4)
+    *reinterpret_cast<float4*>(dst + d0 + e) = make_float4(acc[e], acc[e + 1], acc[e + 2], acc[e + 3]);
+  if (d0 == 0) {
+    dst[128] = mx;
+    dst[129] = lsum;
   }
 }
 
@@ -863,12 +1002,12 @@ int attn_launch(const rb_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t s
   float* part = static_cast<float*>(ws);
   const int nchunks = prefix_nchunks(a->NP, a->H);
   if (nchunks > 0) {
-    if (a->dtype == RB_F32) {  // fp32: CUDA-core FFMA (the 1e-5 parity bar rules out tf32 MMAs)
+    if (a->dtype == RB_F32) {  // fp32: three tf32 products per term on the tensor cores (1e-5 parity bar)
       dim3 grid(nchunks, a->H, (a->M + 15) / 16);
-      if (cudaFuncSetAttribute(attn_prefix_simt<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSimtSmem) !=
+      if (cudaFuncSetAttribute(attn_prefix_tf32, cudaFuncAttributeMaxDynamicSharedMemorySize, t32::kSmemBytes) !=
           cudaSuccess)
         return RB_ERR_CUDA;
-      attn_prefix_simt<float><<<grid, 128, kSimtSmem, stream>>>(p, part, nchunks);
+      attn_prefix_tf32<<<grid, 128, t32::kSmemBytes, stream>>>(p, part);
       if (cudaGetLastError() != cudaSuccess) return RB_ERR_CUDA;
     } else {  // bf16: tcgen05 QK^T / PV with TMA-staged tiles
       CUtensorMap tq, tk, tv;
