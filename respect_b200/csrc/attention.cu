@@ -51,13 +51,13 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t 
 // lo = x - hi): at most about 2^-19 relative error per term, fp32 accumulation
 // (mma.sync.m16n8k8 tf32, independent of the row count).
 //
-// Block = 4 warps = 16 query rows of one head over one prefix chunk. Key tiles
-// of 32 keys are copied into shared memory with cp.async (K two tiles deep: the
-// next tile's K lands during this tile; V one deep: it lands during the S
-// products of its tile); warp w takes keys
-// 8w .. 8w + 7 of every tile (one n-tile of S, one k-step of P·V) and keeps its
-// own online-softmax state, so no warp waits for another within a tile. At the
-// end the four states are merged in warp order into the chunk partial.
+// Block = 4 warps = 16 query rows of one head over one prefix chunk. Warp w
+// takes keys 8w .. 8w + 7 of every 32-key tile (one n-tile of S, one k-step of
+// P·V), copies their K and V rows into its own shared-memory rows with cp.async
+// (the next keys' K lands during the softmax and P·V, their V during the S
+// products) and keeps its own online-softmax state, so the warps never wait for
+// one another until the end, where the four states are merged in warp order
+// into the chunk partial.
 //
 // Fragment layouts (lane = 4g + t): the 128 head dims enter the S products in a
 // fixed permuted order, k-step 2i + o (o = 0, 1) position t <- dim 16i + 4t + 2o
@@ -70,10 +70,10 @@ namespace t32 {
 constexpr int kRows = 16, kTK = 32, kD = 128;
 constexpr int kQP = 144, kKP = 144, kVP = 132;   // shared-memory row pitches (floats): conflict-free fragment reads
 constexpr int kQFloats = kRows * kQP;            // one of Q hi / Q lo
-constexpr int kKFloats = kTK * kKP, kVFloats = kTK * kVP;
-constexpr int kMergeFloats = 4 * kRows * kPartStride;   // the four warps' states (reuses the K area)
-static_assert(kMergeFloats <= 2 * kKFloats, "merge area fits in the K tiles");
-constexpr int kSmemBytes = (2 * kQFloats + 2 * kKFloats + kVFloats) * 4;
+constexpr int kWarpKV = 8 * kKP + 8 * kVP;               // one warp's K and V rows
+constexpr int kMergeFloats = 4 * kRows * kPartStride;   // the four warps' states (reuses the K / V rows)
+static_assert(kMergeFloats <= 4 * kWarpKV, "merge area fits in the K / V rows");
+constexpr int kSmemBytes = (2 * kQFloats + 4 * kWarpKV) * 4;
 }  // namespace t32
 
 __device__ __forceinline__ uint32_t tf32_rna(float x) {
@@ -114,13 +114,16 @@ __global__ void __launch_bounds__(128) attn_prefix_tf32(const AttnDev p, float* 
   extern __shared__ __align__(16) float t32_smem[];
   uint32_t* qh = reinterpret_cast<uint32_t*>(t32_smem);          // [16][kQP] tf32 hi of q
   uint32_t* ql = qh + kQFloats;                                  // [16][kQP] tf32 lo of q
-  float* ks0 = t32_smem + 2 * kQFloats;                          // [2][32][kKP]
-  float* vs = ks0 + 2 * kKFloats;                                // [32][kVP]
+  float* kv0 = t32_smem + 2 * kQFloats;                          // per warp: K [8][kKP], V [8][kVP]
   const int c = blockIdx.x, h = blockIdx.y, r0 = blockIdx.z * kRows;
   const int kvh = h / (p.H / p.HK);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  pdl_trigger();
+  float* ks = kv0 + warp * kWarpKV;   // this warp's K rows
+  float* vs = ks + 8 * kKP;           // and V rows
+  // Dependents (the node kernel) are released only after this grid's wait: they
+  // read q and the node K / V before their own wait.
   pdl_wait();
+  pdl_trigger();
   const int NP = p.sp ? p.sp->prompt_len : p.NP;
   const int M = p.sp ? min(p.M, p.sp->q) : p.M;
   const int C = prefix_chunk(NP, p.H);
@@ -145,34 +148,28 @@ __global__ void __launch_bounds__(128) attn_prefix_tf32(const AttnDev p, float* 
   for (int j = 0; j < 16; ++j)
 #pragma unroll
     for (int e = 0; e < 4; ++e) o[j][e] = 0.f;
-  // K or V rows of the tile at key kt (keys past the chunk end zero-filled), one cp.async group
-  // (thread = row j0 + 4 it, 16 bytes at dim 4 lane: one row per warp per step)
-  auto load_rows = [&](float* dst, int pitch, const float* src, int64_t sh, int64_t sn, int kt) {
-    const int j0 = threadIdx.x >> 5;
-    const float* s0 = src + kvh * sh + static_cast<int64_t>(kt + j0) * sn + 4 * lane;
-    const float* sf = src + kvh * sh + static_cast<int64_t>(k0) * sn + 4 * lane;   // any valid row (zero-filled)
-    float* d0 = dst + j0 * pitch + 4 * lane;
-    const int64_t step = 4 * sn;
+  __syncthreads();   // q visible to every warp
+  // K or V rows of the warp's keys kw .. kw + 7 (keys past the chunk end zero-filled), one cp.async group
+  auto load8 = [&](float* dst, int pitch, const float* src, int64_t sh, int64_t sn, int kw) {
+    const float* base = src + kvh * sh + 4 * lane;
 #pragma unroll
-    for (int it = 0; it < kTK / 4; ++it) {
-      const bool ok = kt + j0 + 4 * it < k1;
-      cp_async16(d0 + it * 4 * pitch, ok ? s0 + it * step : sf, ok ? 16u : 0u);
+    for (int r = 0; r < 8; ++r) {
+      const bool ok = kw + r < k1;
+      cp_async16(dst + r * pitch + 4 * lane, base + static_cast<int64_t>(ok ? kw + r : k0) * sn, ok ? 16u : 0u);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  load_rows(ks0, kKP, kp, p.skph, p.skpn, k0);
-  load_rows(vs, kVP, vp, p.svph, p.svpn, k0);
-  for (int kt = k0, tile = 0; kt < k1; kt += kTK, ++tile) {
-    const float* ks = ks0 + (tile & 1) * kKFloats;
-    // the next tile's K (its buffer was last read by the previous tile's S products)
-    if (kt + kTK < k1) load_rows(ks0 + ((tile + 1) & 1) * kKFloats, kKP, kp, p.skph, p.skpn, kt + kTK);
-    else asm volatile("cp.async.commit_group;" ::: "memory");   // an empty group keeps the counts below
-    asm volatile("cp.async.wait_group 2;" ::: "memory");        // this tile's K (V and the next K may pend)
-    __syncthreads();   // this tile's K (and q) visible to every warp
-    const int kw = kt + warp * 8;   // the warp's first key
-    const bool act = kw < k1;       // uniform per warp
+  if (k0 + warp * 8 < k1) {
+    load8(ks, kKP, kp, p.skph, p.skpn, k0 + warp * 8);
+    load8(vs, kVP, vp, p.svph, p.svpn, k0 + warp * 8);
+  }
+  // The warp's keys of every 32-key tile; warps never wait for one another here.
+  for (int kw = k0 + warp * 8; kw < k1; kw += kTK) {
+    const int kn = kw + kTK;   // the warp's keys in the next tile
+    asm volatile("cp.async.wait_group 1;" ::: "memory");   // this tile's K (its V may pend)
+    __syncwarp();
     uint32_t ph[4], pl[4];          // P of the warp's keys, tf32 hi / lo
-    if (act) {
+    {
       // S (16 rows x the warp's 8 keys). Six independent accumulators (hi·hi,
       // hi·lo, lo·hi, each for even and odd k-steps) keep the MMA chains short;
       // they are added in a fixed order at the end.
@@ -181,7 +178,7 @@ __global__ void __launch_bounds__(128) attn_prefix_tf32(const AttnDev p, float* 
       for (int a = 0; a < 6; ++a)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[a][e] = 0.f;
-      const float* kr = ks + (warp * 8 + g) * kKP + 4 * t;
+      const float* kr = ks + g * kKP + 4 * t;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const uint4 a_g = *reinterpret_cast<const uint4*>(qh + g * kQP + 16 * i + 4 * t);
@@ -205,6 +202,9 @@ __global__ void __launch_bounds__(128) attn_prefix_tf32(const AttnDev p, float* 
       float s[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) s[e] = (acc[0][e] + acc[1][e]) + ((acc[2][e] + acc[3][e]) + (acc[4][e] + acc[5][e]));
+      __syncwarp();   // every lane is done with this tile's K
+      if (kn < k1) load8(ks, kKP, kp, p.skph, p.skpn, kn);
+      else asm volatile("cp.async.commit_group;" ::: "memory");   // an empty group keeps the counts
       // online softmax over the 8 keys (rows g: s[0], s[1]; rows g + 8: s[2], s[3])
       const bool v0 = kw + 2 * t < k1, v1 = kw + 2 * t + 1 < k1;
       s[0] = v0 ? s[0] * scale2 : -INFINITY;
@@ -243,9 +243,9 @@ __global__ void __launch_bounds__(128) attn_prefix_tf32(const AttnDev p, float* 
       split_tf32_fast(p3, ph[3], pl[3]);   // (g + 8, key 2t + 1)
     }
     asm volatile("cp.async.wait_group 1;" ::: "memory");   // this tile's V (the next K may pend)
-    __syncthreads();   // this tile's V visible to every warp
-    if (act) {   // O += P V
-      const float* v0r = vs + (warp * 8 + 2 * t) * kVP + 4 * g;
+    __syncwarp();
+    {   // O += P V
+      const float* v0r = vs + (2 * t) * kVP + 4 * g;
       const float* v1r = v0r + kVP;
 #pragma unroll
       for (int jq = 0; jq < 4; ++jq) {
@@ -261,12 +261,14 @@ __global__ void __launch_bounds__(128) attn_prefix_tf32(const AttnDev p, float* 
         }
       }
     }
-    __syncthreads();   // every warp is done with this tile's V (and K) before they are overwritten
-    if (kt + kTK < k1) load_rows(vs, kVP, vp, p.svph, p.svpn, kt + kTK);
+    __syncwarp();   // every lane is done with this tile's V
+    if (kn < k1) load8(vs, kVP, vp, p.svph, p.svpn, kn);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");   // nothing in flight into the merge area
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();   // every warp is done with its K / V rows: the merge area reuses them
   // merge the four warps' states in warp order: O = sum_w O_w 2^(m_w - m), l likewise
-  float* st = ks0;   // [4][16][kPartStride]: O at dims 0..127, m at 128, l at 129
+  float* st = kv0;   // [4][16][kPartStride]: O at dims 0..127, m at 128, l at 129
   float* mine = st + warp * kRows * kPartStride;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
@@ -1019,8 +1021,10 @@ int attn_launch(const rb_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t s
       if (st != RB_OK) return st;
     }
   }
-  if (a->dtype == RB_F32) return launch_nodes<float>(p, part, stream, false);
-  return launch_nodes<uint16_t>(p, part, stream, false);
+  // The node kernel follows under PDL: its folds (q and node K / V only) run
+  // beside the prefix kernel, its merges wait for the prefix partials.
+  if (a->dtype == RB_F32) return launch_nodes<float>(p, part, stream, nchunks > 0);
+  return launch_nodes<uint16_t>(p, part, stream, nchunks > 0);
 }
 
 // Engine path: bf16, q/base/PL from device memory, trie masking from the ancestor chains.
