@@ -376,7 +376,10 @@ def run_native(args):
         + NODES * cfg.vocab * 4
     roof = {"bound": "hbm", "kernel": "gemm_kernel<256,1,kEpiSiluMul> fused gate|up+SiLU*mul N=37888 K=3584 M=128",
             "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "peak_source": src,
-            "traffic": profiled_traffic(), "algorithmic_bytes": gu_bytes, "launch_ms": gu_ms}
+            "traffic": profiled_traffic(),
+            "traffic_source": "committed ncu capture of this kernel (profiles/gemm_gate_up_config3.md), "
+                              "not a per-run measurement",
+            "algorithmic_bytes": gu_bytes, "launch_ms": gu_ms}
     step_roof = {"bound": "hbm", "algorithmic_bytes": step_bytes, "achieved": step_bytes / (ms_step * 1e-3) / 1e9,
                  "peak": hbm, "unit": "GB/s", "frac": step_bytes / (ms_step * 1e-3) / 1e9 / hbm,
                  "floor_ms": step_bytes / (hbm * 1e9) * 1e3}
