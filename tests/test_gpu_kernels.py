@@ -66,6 +66,33 @@ def test_attention_bf16_vs_oracle(NP, committed):
     assert np.abs(got - eager).max() < 2e-2
 
 
+@pytest.mark.parametrize("NP,committed", [(1, 0), (31, 2), (33, 0), (700, 5), (3000, 37)])
+def test_attention_fp32_vs_oracle_and_row_invariance(NP, committed):
+    """fp32 path (three tf32 products per term) at prefix lengths that leave partial
+    32-key tiles and key groups without keys: within 1e-5 of the oracle and of
+    eager, and every row alone bitwise equal to its row of the full call."""
+    from respect_b200.kernels.attention import attn_call, fused_attn_hyb
+    rng = np.random.default_rng(NP + 11 * committed)
+    seqs = top_up(rng, chain_seqs(rng, 4, 32, 50), 128, 50)
+    c = attention_case(5, H=28, HK=4, NP=NP, seqs=seqs, committed=committed)
+    q, msk = pad_rows(c)
+    out = fused_attn_hyb(T(q), T(c["kp"]), T(c["vp"]), T(c["kn"]), T(c["vn"]), T(msk, torch.bool))
+    M = c["q"].shape[1]
+    got = out[:, :M].cpu().numpy()
+    ref = oatt.fused_attn_hyb(c["q"], c["kp"], c["vp"], c["kn"], c["vn"], c["msk"])
+    assert np.abs(got - ref).max() < 1e-5
+    eager = oatt.sdpa(c["q"], c["kp"], c["vp"], c["kn"], c["vn"], c["msk"])
+    assert np.abs(got - eager).max() < 1e-5
+    full = torch.empty(28, M, 128, device=DEV)
+    t = {k: T(c[k]) for k in ("q", "kp", "vp", "kn", "vn")}
+    mt = T(c["msk"], torch.bool)
+    attn_call(t["q"], t["kp"], t["vp"], t["kn"], t["vn"], mt, full, 128 ** -0.5)
+    for r in (0, 15, 16, M - 1):
+        o1 = torch.empty(28, 1, 128, device=DEV)
+        attn_call(t["q"][:, r:r + 1], t["kp"], t["vp"], t["kn"], t["vn"], mt[r:r + 1], o1, 128 ** -0.5)
+        assert torch.equal(o1[:, 0], full[:, r])
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_attention_slot_layout_invariance(dtype):
     """The reference's own check (tests/test_kernel_invariance.py:30-54): the same 26
