@@ -54,8 +54,8 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t 
 // Block = 4 warps = 16 query rows of one head over one prefix chunk. Warp w
 // takes keys 8w .. 8w + 7 of every 32-key tile (one n-tile of S, one k-step of
 // P·V), copies their K and V rows into its own shared-memory rows with cp.async
-// (the next keys' K lands during the softmax and P·V, their V during the S
-// products) and keeps its own online-softmax state, so the warps never wait for
+// (software-pipelined: S of the next keys runs before P·V of the current ones)
+// and keeps its own online-softmax state, so the warps never wait for
 // one another until the end, where the four states are merged in warp order
 // into the chunk partial.
 //
@@ -162,111 +162,136 @@ __global__ void __launch_bounds__(32 * t32::kWarps) attn_prefix_tf32(const AttnD
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  if (k0 + warp * 8 < k1) {
-    load8(ks, kKP, kp, p.skph, p.skpn, k0 + warp * 8);
-    load8(vs, kVP, vp, p.svph, p.svpn, k0 + warp * 8);
+  // S of the warp's keys kw .. kw + 7 into s (16 rows x 8 keys)
+  auto s_products = [&](float (&s)[4]) {
+    // S (16 rows x the warp's 8 keys). Six independent accumulators (hi·hi,
+    // hi·lo, lo·hi, each for even and odd k-steps) keep the MMA chains short;
+    // they are added in a fixed order at the end.
+    float acc[6][4];
+#pragma unroll
+    for (int a = 0; a < 6; ++a)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[a][e] = 0.f;
+    const float* kr = ks + g * kKP + 4 * t;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint4 a_g = *reinterpret_cast<const uint4*>(qh + g * kQP + 16 * i + 4 * t);
+      const uint4 a_g8 = *reinterpret_cast<const uint4*>(qh + (g + 8) * kQP + 16 * i + 4 * t);
+      const uint4 b_g = *reinterpret_cast<const uint4*>(ql + g * kQP + 16 * i + 4 * t);
+      const uint4 b_g8 = *reinterpret_cast<const uint4*>(ql + (g + 8) * kQP + 16 * i + 4 * t);
+      const float4 kv = *reinterpret_cast<const float4*>(kr + 16 * i);
+      uint32_t kh[4], kl[4];
+      split_tf32_fast(kv.x, kh[0], kl[0]);
+      split_tf32_fast(kv.y, kh[1], kl[1]);
+      split_tf32_fast(kv.z, kh[2], kl[2]);
+      split_tf32_fast(kv.w, kh[3], kl[3]);
+      // k-step 2i: dims 16i + 4t + {0, 1}; k-step 2i + 1: dims 16i + 4t + {2, 3}
+      mma_tf32_1688(acc[0], a_g.x, a_g8.x, a_g.y, a_g8.y, kh[0], kh[1]);
+      mma_tf32_1688(acc[1], a_g.z, a_g8.z, a_g.w, a_g8.w, kh[2], kh[3]);
+      mma_tf32_1688(acc[2], a_g.x, a_g8.x, a_g.y, a_g8.y, kl[0], kl[1]);
+      mma_tf32_1688(acc[3], a_g.z, a_g8.z, a_g.w, a_g8.w, kl[2], kl[3]);
+      mma_tf32_1688(acc[4], b_g.x, b_g8.x, b_g.y, b_g8.y, kh[0], kh[1]);
+      mma_tf32_1688(acc[5], b_g.z, b_g8.z, b_g.w, b_g8.w, kh[2], kh[3]);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[e] = (acc[0][e] + acc[1][e]) + ((acc[2][e] + acc[3][e]) + (acc[4][e] + acc[5][e]));
+  };
+  // online softmax of those keys; P (tf32 hi / lo) into ph / pl
+  uint32_t ph[4], pl[4];
+  auto softmax_step = [&](int kw, float (&s)[4]) {
+    // online softmax over the 8 keys (rows g: s[0], s[1]; rows g + 8: s[2], s[3])
+    const bool v0 = kw + 2 * t < k1, v1 = kw + 2 * t + 1 < k1;
+    s[0] = v0 ? s[0] * scale2 : -INFINITY;
+    s[1] = v1 ? s[1] * scale2 : -INFINITY;
+    s[2] = v0 ? s[2] * scale2 : -INFINITY;
+    s[3] = v1 ? s[3] * scale2 : -INFINITY;
+    float x0 = fmaxf(s[0], s[1]), x1 = fmaxf(s[2], s[3]);
+    x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, 1));
+    x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, 2));
+    x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, 1));
+    x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, 2));
+    const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);   // finite: the warp's first key is valid
+    const float al0 = fast_exp2(m0 - n0), al1 = fast_exp2(m1 - n1);
+    const float p0 = fast_exp2(s[0] - n0), p1 = fast_exp2(s[1] - n0);
+    const float p2 = fast_exp2(s[2] - n1), p3 = fast_exp2(s[3] - n1);
+    float rs0 = p0 + p1, rs1 = p2 + p3;
+    rs0 += __shfl_xor_sync(0xffffffffu, rs0, 1);
+    rs0 += __shfl_xor_sync(0xffffffffu, rs0, 2);
+    rs1 += __shfl_xor_sync(0xffffffffu, rs1, 1);
+    rs1 += __shfl_xor_sync(0xffffffffu, rs1, 2);
+    l0 = fmaf(l0, al0, rs0);
+    l1 = fmaf(l1, al1, rs1);
+    m0 = n0;
+    m1 = n1;
+    if (!__all_sync(0xffffffffu, al0 == 1.f && al1 == 1.f)) {   // the warp's running maxima moved
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        o[j][0] *= al0; o[j][1] *= al0;
+        o[j][2] *= al1; o[j][3] *= al1;
+      }
+    }
+    // A of P V = P in key order (2t, 2t + 1) -> positions (t, t + 4)
+    split_tf32_fast(p0, ph[0], pl[0]);   // (g, key 2t)
+    split_tf32_fast(p2, ph[1], pl[1]);   // (g + 8, key 2t)
+    split_tf32_fast(p1, ph[2], pl[2]);   // (g, key 2t + 1)
+    split_tf32_fast(p3, ph[3], pl[3]);   // (g + 8, key 2t + 1)
+  };
+  // O += P V of the keys whose V rows are staged
+  auto pv_step = [&]() {
+    const float* v0r = vs + (2 * t) * kVP + 4 * g;
+    const float* v1r = v0r + kVP;
+#pragma unroll
+    for (int jq = 0; jq < 4; ++jq) {
+      const float4 va = *reinterpret_cast<const float4*>(v0r + 32 * jq);
+      const float4 vb = *reinterpret_cast<const float4*>(v1r + 32 * jq);
+      const float a4[4] = {va.x, va.y, va.z, va.w}, b4[4] = {vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+      for (int jr = 0; jr < 4; ++jr) {
+        uint32_t h0, l0b, h1, l1b;
+        split_tf32_fast(a4[jr], h0, l0b);
+        split_tf32_fast(b4[jr], h1, l1b);
+        mma_3xtf32(o[jq * 4 + jr], ph, pl, h0, h1, l0b, l1b);
+      }
+    }
+  };
+  // Software-pipelined over the warp's tiles: S of the next keys runs before
+  // P·V of the current ones, so each V load lands during a softmax and the
+  // next S products, each K load during a P·V and a softmax.
+  // cp.async groups in flight at each wait: K(next), V(current).
+  const int kfirst = k0 + warp * 8;
+  if (kfirst < k1) {
+    load8(ks, kKP, kp, p.skph, p.skpn, kfirst);
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncwarp();
+    float s[4];
+    s_products(s);
+    __syncwarp();   // every lane is done with these K rows
+    if (kfirst + kTK < k1) load8(ks, kKP, kp, p.skph, p.skpn, kfirst + kTK);
+    else asm volatile("cp.async.commit_group;" ::: "memory");   // an empty group keeps the counts
+    load8(vs, kVP, vp, p.svph, p.svpn, kfirst);
+    softmax_step(kfirst, s);
   }
-  // The warp's keys of every 32-key tile; warps never wait for one another here.
-  for (int kw = k0 + warp * 8; kw < k1; kw += kTK) {
+  for (int kw = kfirst; kw < k1; kw += kTK) {
     const int kn = kw + kTK;   // the warp's keys in the next tile
-    asm volatile("cp.async.wait_group 1;" ::: "memory");   // this tile's K (its V may pend)
-    __syncwarp();
-    uint32_t ph[4], pl[4];          // P of the warp's keys, tf32 hi / lo
-    {
-      // S (16 rows x the warp's 8 keys). Six independent accumulators (hi·hi,
-      // hi·lo, lo·hi, each for even and odd k-steps) keep the MMA chains short;
-      // they are added in a fixed order at the end.
-      float acc[6][4];
-#pragma unroll
-      for (int a = 0; a < 6; ++a)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[a][e] = 0.f;
-      const float* kr = ks + g * kKP + 4 * t;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint4 a_g = *reinterpret_cast<const uint4*>(qh + g * kQP + 16 * i + 4 * t);
-        const uint4 a_g8 = *reinterpret_cast<const uint4*>(qh + (g + 8) * kQP + 16 * i + 4 * t);
-        const uint4 b_g = *reinterpret_cast<const uint4*>(ql + g * kQP + 16 * i + 4 * t);
-        const uint4 b_g8 = *reinterpret_cast<const uint4*>(ql + (g + 8) * kQP + 16 * i + 4 * t);
-        const float4 kv = *reinterpret_cast<const float4*>(kr + 16 * i);
-        uint32_t kh[4], kl[4];
-        split_tf32_fast(kv.x, kh[0], kl[0]);
-        split_tf32_fast(kv.y, kh[1], kl[1]);
-        split_tf32_fast(kv.z, kh[2], kl[2]);
-        split_tf32_fast(kv.w, kh[3], kl[3]);
-        // k-step 2i: dims 16i + 4t + {0, 1}; k-step 2i + 1: dims 16i + 4t + {2, 3}
-        mma_tf32_1688(acc[0], a_g.x, a_g8.x, a_g.y, a_g8.y, kh[0], kh[1]);
-        mma_tf32_1688(acc[1], a_g.z, a_g8.z, a_g.w, a_g8.w, kh[2], kh[3]);
-        mma_tf32_1688(acc[2], a_g.x, a_g8.x, a_g.y, a_g8.y, kl[0], kl[1]);
-        mma_tf32_1688(acc[3], a_g.z, a_g8.z, a_g.w, a_g8.w, kl[2], kl[3]);
-        mma_tf32_1688(acc[4], b_g.x, b_g8.x, b_g.y, b_g8.y, kh[0], kh[1]);
-        mma_tf32_1688(acc[5], b_g.z, b_g8.z, b_g.w, b_g8.w, kh[2], kh[3]);
-      }
-      float s[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) s[e] = (acc[0][e] + acc[1][e]) + ((acc[2][e] + acc[3][e]) + (acc[4][e] + acc[5][e]));
-      __syncwarp();   // every lane is done with this tile's K
-      if (kn < k1) load8(ks, kKP, kp, p.skph, p.skpn, kn);
-      else asm volatile("cp.async.commit_group;" ::: "memory");   // an empty group keeps the counts
-      // online softmax over the 8 keys (rows g: s[0], s[1]; rows g + 8: s[2], s[3])
-      const bool v0 = kw + 2 * t < k1, v1 = kw + 2 * t + 1 < k1;
-      s[0] = v0 ? s[0] * scale2 : -INFINITY;
-      s[1] = v1 ? s[1] * scale2 : -INFINITY;
-      s[2] = v0 ? s[2] * scale2 : -INFINITY;
-      s[3] = v1 ? s[3] * scale2 : -INFINITY;
-      float x0 = fmaxf(s[0], s[1]), x1 = fmaxf(s[2], s[3]);
-      x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, 1));
-      x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, 2));
-      x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, 1));
-      x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, 2));
-      const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);   // finite: the warp's first key is valid
-      const float al0 = fast_exp2(m0 - n0), al1 = fast_exp2(m1 - n1);
-      const float p0 = fast_exp2(s[0] - n0), p1 = fast_exp2(s[1] - n0);
-      const float p2 = fast_exp2(s[2] - n1), p3 = fast_exp2(s[3] - n1);
-      float rs0 = p0 + p1, rs1 = p2 + p3;
-      rs0 += __shfl_xor_sync(0xffffffffu, rs0, 1);
-      rs0 += __shfl_xor_sync(0xffffffffu, rs0, 2);
-      rs1 += __shfl_xor_sync(0xffffffffu, rs1, 1);
-      rs1 += __shfl_xor_sync(0xffffffffu, rs1, 2);
-      l0 = fmaf(l0, al0, rs0);
-      l1 = fmaf(l1, al1, rs1);
-      m0 = n0;
-      m1 = n1;
-      if (!__all_sync(0xffffffffu, al0 == 1.f && al1 == 1.f)) {   // the warp's running maxima moved
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          o[j][0] *= al0; o[j][1] *= al0;
-          o[j][2] *= al1; o[j][3] *= al1;
-        }
-      }
-      // A of P V = P in key order (2t, 2t + 1) -> positions (t, t + 4)
-      split_tf32_fast(p0, ph[0], pl[0]);   // (g, key 2t)
-      split_tf32_fast(p2, ph[1], pl[1]);   // (g + 8, key 2t)
-      split_tf32_fast(p1, ph[2], pl[2]);   // (g, key 2t + 1)
-      split_tf32_fast(p3, ph[3], pl[3]);   // (g + 8, key 2t + 1)
+    float s[4];
+    if (kn < k1) {
+      asm volatile("cp.async.wait_group 1;" ::: "memory");   // K(next) (V(current) may pend)
+      __syncwarp();
+      s_products(s);
+      __syncwarp();
+      if (kn + kTK < k1) load8(ks, kKP, kp, p.skph, p.skpn, kn + kTK);
+      else asm volatile("cp.async.commit_group;" ::: "memory");
+    } else {
+      asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    asm volatile("cp.async.wait_group 1;" ::: "memory");   // this tile's V (the next K may pend)
+    asm volatile("cp.async.wait_group 1;" ::: "memory");     // V(current)
     __syncwarp();
-    {   // O += P V
-      const float* v0r = vs + (2 * t) * kVP + 4 * g;
-      const float* v1r = v0r + kVP;
-#pragma unroll
-      for (int jq = 0; jq < 4; ++jq) {
-        const float4 va = *reinterpret_cast<const float4*>(v0r + 32 * jq);
-        const float4 vb = *reinterpret_cast<const float4*>(v1r + 32 * jq);
-        const float a4[4] = {va.x, va.y, va.z, va.w}, b4[4] = {vb.x, vb.y, vb.z, vb.w};
-#pragma unroll
-        for (int jr = 0; jr < 4; ++jr) {
-          uint32_t h0, l0b, h1, l1b;
-          split_tf32_fast(a4[jr], h0, l0b);
-          split_tf32_fast(b4[jr], h1, l1b);
-          mma_3xtf32(o[jq * 4 + jr], ph, pl, h0, h1, l0b, l1b);
-        }
-      }
+    pv_step();
+    __syncwarp();   // every lane is done with these V rows
+    if (kn < k1) {
+      load8(vs, kVP, vp, p.svph, p.svpn, kn);
+      softmax_step(kn, s);
     }
-    __syncwarp();   // every lane is done with this tile's V
-    if (kn < k1) load8(vs, kVP, vp, p.svph, p.svpn, kn);
-    else asm volatile("cp.async.commit_group;" ::: "memory");
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();   // every warp is done with its K / V rows: the merge area reuses them
