@@ -4,13 +4,16 @@
 // C = prefix_chunk(NP, H) keys at ABSOLUTE positions (chunk c = [c*C, (c+1)*C)), each
 // chunk reduced by an online softmax over fixed key tiles into a partial
 // (max, sum, acc[D]) per query row. Chunk boundaries depend on NP only.
-// Phase 2 (per query row, one warp): merge the chunk partials in chunk order,
-// then visit node slots 0..NN-1 in slot order and fold in every ALLOWED slot
-// one at a time (score, online-softmax update, acc += p*v, all fp32). Masked
-// slots are skipped, which is exactly what the reference's -inf scores do
-// (exp(-inf) = 0, alpha = 1), so a row's result depends only on the values of
+// Phase 2 (per query row and kv head, one warp): fold the row's ALLOWED node
+// keys in their list order (committed slots, then trie ancestors; or slot order
+// in the mask modes), in batches cut at fixed list positions, into a node
+// partial; then merge the chunk partials in chunk order and the node partial.
+// Masked slots are skipped, which is exactly what the reference's -inf scores
+// do (exp(-inf) = 0, alpha = 1), so a row's result depends only on the values of
 // its allowed keys and their order, never on where siblings sit in the buffer
-// or on how many rows the call carries. Final acc / l, one cast.
+// or on how many rows the call carries. Final acc / l, one cast. Both phases run
+// on the tensor cores: bf16 products (tcgen05 / mma.sync), or for fp32 data three
+// tf32 products per term.
 #include "attention.cuh"
 #include "common.cuh"
 #include "host_util.h"
@@ -359,72 +362,15 @@ __device__ __forceinline__ bool node_allowed(const AttnDev& p, int row, int j) {
   }
 }
 
-// Node phase. A row's allowed node slots are visited in slot order, in
-// batches of up to 32. Lane u scores the batch's u-th slot (q.k over the 128
-// dims in a fixed order: four interleaved partial sums over d = 4c + e, added
-// pairwise; times scale*log2(e)), then the batch is folded
-// one slot at a time, starting from an empty state:
-//   m' = max(m, s); a = 2^(m - m'); p = 2^(s - m'); acc = p*v + acc*a; l = l*a + p
-// (lane u of the fold owns dims [4u, 4u+4)). Every slot goes through exactly
-// this arithmetic whatever the masking mode or batch boundaries, so the node
-// partial of a row depends only on its allowed slots and their order. The
-// output is then merge(prefix chunk 0, 1, ..., node partial), in that order.
-//
-// One item = one query row x one kv head; warp g serves query head kvh*G + g
-// (G = H / HK). The row's slots (committed, then trie ancestors, or the
-// allowed mask entries) are the same for all G heads, so each batch of node
-// K / V rows is staged in shared memory once for the whole group. A block
-// runs R items: their node folds before griddepcontrol.wait (they need only
-// q and the node K / V, which the kernel before the prefix kernel wrote, so
-// under PDL they run while the prefix kernel is still working), the merges
+// Node phase. One item = one query row x one kv head (the G = H / HK query
+// heads of the kv head together). A row's key list (committed slots, then its
+// trie ancestors; or the slots its mask allows, in slot order) is folded in
+// batches cut at fixed list positions, so a row's node partial depends only on
+// its keys and their order; the output is merge(prefix chunk 0, 1, ..., node
+// partial), in that order. The folds need only q and the node K / V, so they run
+// before griddepcontrol.wait (under PDL, beside the prefix kernel); the merges
 // with the prefix chunk partials after it.
-constexpr int kMaxGroup = 16;   // query heads per kv head handled by one block
-
-template <typename T>
-struct NodeSmem {
-  static constexpr int kRow = 128 * static_cast<int>(sizeof(T));  // bytes of one K / V row
-  static constexpr int kKPitch = kRow + 16;                         // padded: conflict-free lane-per-row reads
-  static constexpr int kStage = 32 * (kKPitch + kRow);              // one batch of K and V rows
-  __host__ __device__ static int bytes(int G) { return kStage + G * 128 * 4; }   // + q of each head (fp32)
-};
-
-template <typename T>
-__device__ __forceinline__ float dot128_smem(const uint8_t* krow, const float* qs);
-template <>
-__device__ __forceinline__ float dot128_smem<uint16_t>(const uint8_t* krow, const float* qs) {
-  // four partial sums over d = 4c + e (fixed order), added pairwise at the end
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-  for (int c = 0; c < 16; ++c) {
-    const uint4 k8 = reinterpret_cast<const uint4*>(krow)[c];
-    const float4 qa = reinterpret_cast<const float4*>(qs)[2 * c];
-    const float4 qb = reinterpret_cast<const float4*>(qs)[2 * c + 1];
-    s0 = fmaf(qa.x, bf16_bits_to_f32(static_cast<uint16_t>(k8.x)), s0);
-    s1 = fmaf(qa.y, bf16_bits_to_f32(static_cast<uint16_t>(k8.x >> 16)), s1);
-    s2 = fmaf(qa.z, bf16_bits_to_f32(static_cast<uint16_t>(k8.y)), s2);
-    s3 = fmaf(qa.w, bf16_bits_to_f32(static_cast<uint16_t>(k8.y >> 16)), s3);
-    s0 = fmaf(qb.x, bf16_bits_to_f32(static_cast<uint16_t>(k8.z)), s0);
-    s1 = fmaf(qb.y, bf16_bits_to_f32(static_cast<uint16_t>(k8.z >> 16)), s1);
-    s2 = fmaf(qb.z, bf16_bits_to_f32(static_cast<uint16_t>(k8.w)), s2);
-    s3 = fmaf(qb.w, bf16_bits_to_f32(static_cast<uint16_t>(k8.w >> 16)), s3);
-  }
-  return (s0 + s1) + (s2 + s3);
-}
-template <>
-__device__ __forceinline__ float dot128_smem<float>(const uint8_t* krow, const float* qs) {
-  // four partial sums over d = 4c + e (fixed order), added pairwise at the end
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-  for (int c = 0; c < 32; ++c) {
-    const float4 k4 = reinterpret_cast<const float4*>(krow)[c];
-    const float4 q4 = reinterpret_cast<const float4*>(qs)[c];
-    s0 = fmaf(q4.x, k4.x, s0);
-    s1 = fmaf(q4.y, k4.y, s1);
-    s2 = fmaf(q4.z, k4.z, s2);
-    s3 = fmaf(q4.w, k4.w, s3);
-  }
-  return (s0 + s1) + (s2 + s3);
-}
+constexpr int kMaxGroup = 16;   // query heads per kv head: one m16 tile of rows
 
 // Running softmax state of one (row, head), lane-owned dims [4*lane, 4*lane+4).
 struct NodeAcc {
@@ -441,190 +387,6 @@ __device__ __forceinline__ void merge_into(NodeAcc& a, float bm, float bl, const
   for (int e = 0; e < 4; ++e) a.acc[e] = fmaf(bacc[e], y, a.acc[e] * x);
   a.l = fmaf(bl, y, a.l * x);
   a.m = m_new;
-}
-
-// The node fold of one item (block-uniform arguments; contains __syncthreads).
-template <typename T>
-__device__ NodeAcc node_fold(const AttnDev& p, int row, int kvh, uint8_t* smem, int* slots, int* nslots) {
-  using L = NodeSmem<T>;
-  auto ks = reinterpret_cast<uint8_t(*)[L::kKPitch]>(smem);
-  auto vs = reinterpret_cast<uint8_t(*)[L::kRow]>(smem + 32 * L::kKPitch);
-  const int G = p.H / p.HK;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nthr = G * 32;
-  const int d0 = lane * 4;
-  float* qs = reinterpret_cast<float*>(smem + L::kStage) + warp * 128;
-  const int h = kvh * G + warp;
-  const int NP = p.sp ? p.sp->prompt_len : p.NP;
-  // Node slot 0 sits right after the prefix; without explicit node tensors
-  // (engine path) the node segment is the same buffer from key NP on.
-  const T* kn = p.kn ? static_cast<const T*>(p.kn) : static_cast<const T*>(p.kp) + static_cast<int64_t>(NP) * p.skpn;
-  const T* vn = p.vn ? static_cast<const T*>(p.vn) : static_cast<const T*>(p.vp) + static_cast<int64_t>(NP) * p.svpn;
-  const int64_t kbase = static_cast<int64_t>(kvh) * p.sknh, vbase = static_cast<int64_t>(kvh) * p.svnh;
-  const bool trie = p.mask_kind == kMaskTrie;
-  int base = 0, depth = -1;
-  const int32_t* chain = nullptr;
-  if (trie) {
-    base = p.sp ? p.sp->base : p.causal_first;
-    depth = p.depths[row];
-    if (depth < 0 || depth > row || depth >= p.chain_ld) depth = -1;  // invalid trie: reported when the chain was built
-    chain = p.chain + static_cast<int64_t>(row) * p.chain_ld;
-  }
-  float qv[4];
-  ld4(static_cast<const T*>(p.q) + h * p.sqh + static_cast<int64_t>(row) * p.sqm + d0, qv);
-  *reinterpret_cast<float4*>(qs + d0) = make_float4(qv[0], qv[1], qv[2], qv[3]);
-  __syncwarp();
-
-  NodeAcc r{-INFINITY, 0.f, {0.f, 0.f, 0.f, 0.f}};
-  const float scale2 = p.sm_scale * kLog2e;
-  const int total = trie ? base + depth + 1 : p.NN;
-  for (int b0 = 0; b0 < total; b0 += 32) {
-    // 1. this batch's slots (in slot order)
-    __syncthreads();  // previous batch fully consumed
-    if (warp == 0) {
-      const int i = b0 + lane;
-      int slot = 0;
-      bool v;
-      if (trie) {
-        // the chain entry is read whether or not i < total (its address does not
-        // depend on the depth, so this load does not wait for the depth's)
-        const int ci = i - base;
-        const int cv = (ci >= 0 && ci < p.chain_ld) ? chain[ci] : 0;
-        v = i < total;
-        slot = i < base ? i : base + cv;
-      } else {
-        v = i < p.NN && node_allowed(p, row, i);
-        slot = i;
-      }
-      const unsigned bits = __ballot_sync(0xffffffffu, v);
-      if (v) slots[__popc(bits & ((1u << lane) - 1u))] = slot;
-      if (lane == 0) *nslots = __popc(bits);
-    }
-    __syncthreads();
-    const int cnt = *nslots;
-    if (cnt == 0) continue;
-    // 2. stage the K / V rows of the batch (16-byte pieces, all threads)
-    constexpr int kPieces = L::kRow / 16;
-    for (int t = threadIdx.x; t < cnt * kPieces; t += nthr) {
-      const int u = t / kPieces, pc = t % kPieces;
-      const int64_t sl = slots[u];
-      cp_async16(&ks[u][pc * 16], reinterpret_cast<const uint8_t*>(kn + kbase + sl * p.sknn) + pc * 16, 16u);
-      cp_async16(&vs[u][pc * 16], reinterpret_cast<const uint8_t*>(vn + vbase + sl * p.svnn) + pc * 16, 16u);
-    }
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
-    // 3. scores (lane u <- slot u), then the ordered fold. The running max after
-    // each slot, m_u = max(m, s_0, ..., s_u), comes from a warp scan (max is exact,
-    // so it is the same value a one-slot-at-a-time loop reaches), and lane u forms
-    // its slot's weights a_u = 2^(m_{u-1} - m_u), p_u = 2^(s_u - m_u) in parallel;
-    // only the accumulation below runs slot by slot, in slot order:
-    //   acc = p_u v_u + acc a_u, l = l a_u + p_u
-    const float sc = lane < cnt ? dot128_smem<T>(&ks[lane][0], qs) * scale2 : -INFINITY;
-    float run = sc;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const float y = __shfl_up_sync(0xffffffffu, run, d);
-      if (lane >= d) run = fmaxf(run, y);
-    }
-    const float m_u = fmaxf(r.m, run);
-    float m_prev = __shfl_up_sync(0xffffffffu, m_u, 1);
-    if (lane == 0) m_prev = r.m;
-    const float a_u = fast_exp2(m_prev - m_u);
-    const float p_u = fast_exp2(sc - m_u);
-#pragma unroll 4
-    for (int u = 0; u < cnt; ++u) {
-      const float a = __shfl_sync(0xffffffffu, a_u, u);
-      const float pe = __shfl_sync(0xffffffffu, p_u, u);
-      float vv[4];
-      ld4(reinterpret_cast<const T*>(&vs[u][0]) + d0, vv);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) r.acc[e] = fmaf(pe, vv[e], r.acc[e] * a);
-      r.l = fmaf(r.l, a, pe);
-    }
-    r.m = __shfl_sync(0xffffffffu, m_u, cnt - 1);
-  }
-  return r;
-}
-
-// 48 registers a thread: a block of 7 warps then fits in the register-file
-// partitions a prefix CTA (10 warps at ~136 registers) leaves free, so under
-// PDL one node block per SM folds while the prefix kernel runs (at 64
-// registers none could: two of its warps exceed what is left in a partition).
-template <typename T, int R>
-__global__ void __maxnreg__(48) attn_nodes(const AttnDev p, const float* __restrict__ part) {
-  constexpr int D = 128;
-  __shared__ int slots[32];
-  __shared__ int nslots;
-  extern __shared__ __align__(16) uint8_t node_smem[];  // NodeSmem<T>::bytes(G)
-  const int G = p.H / p.HK;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int d0 = lane * 4;
-  const int live = p.sp ? p.sp->q : p.M;
-  const int n_items = p.M * p.HK;  // item i: row i % M, kv head i / M
-  pdl_trigger();
-
-  NodeAcc nd[R];
-#pragma unroll
-  for (int it = 0; it < R; ++it) {
-    nd[it] = NodeAcc{-INFINITY, 0.f, {0.f, 0.f, 0.f, 0.f}};
-    const int item = blockIdx.x + it * gridDim.x;
-    if (item < n_items && item % p.M < live)  // uniform per block
-      nd[it] = node_fold<T>(p, item % p.M, item / p.M, node_smem, slots, &nslots);
-  }
-
-  pdl_wait();  // the prefix chunk partials are complete
-  const int NP = p.sp ? p.sp->prompt_len : p.NP;
-  const int nchunks = prefix_nchunks(NP, p.H);
-  // The chunk partials of a row (every head of the group) are copied into shared
-  // memory (the fold's staging area, free now) with all copies in flight, as many
-  // chunks as fit at a time; then warp g merges its head's pieces in chunk order.
-  constexpr int kPiece = kPartStride * 4;   // one (chunk, head, row) partial: 528 bytes
-  float* pieces = reinterpret_cast<float*>(node_smem);
-  // chunks staged per round: at least 2 for every group size up to kMaxGroup
-  const int cap = max(1, NodeSmem<T>::bytes(G) / kPiece / G);
-#pragma unroll
-  for (int it = 0; it < R; ++it) {
-    const int item = blockIdx.x + it * gridDim.x;
-    if (item >= n_items) continue;   // uniform per block
-    const int row = item % p.M, kvh = item / p.M, h = kvh * G + warp;
-    T* out = static_cast<T*>(p.out) + h * p.soh + static_cast<int64_t>(row) * p.som + d0;
-    if (row >= live) {  // padding row of a bucketed engine step: zeros, no reads
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        if (sizeof(T) == 2) reinterpret_cast<uint16_t*>(out)[e] = 0;
-        else reinterpret_cast<float*>(out)[e] = 0.f;
-      }
-      continue;
-    }
-    // Prefix chunk partials in ascending chunk order, then the node partial.
-    NodeAcc r{-INFINITY, 0.f, {0.f, 0.f, 0.f, 0.f}};
-    for (int c0 = 0; c0 < nchunks; c0 += cap) {
-      const int nc = min(cap, nchunks - c0);
-      __syncthreads();   // the fold's (or the previous round's) reads of this area are done
-      for (int t = threadIdx.x; t < nc * G * (kPiece / 16); t += blockDim.x) {
-        const int pc = t % (kPiece / 16), pi = t / (kPiece / 16);   // piece pi = (chunk c0 + pi / G, head pi % G)
-        const int c = c0 + pi / G, g = pi % G;
-        const float* src = part + ((static_cast<int64_t>(c) * p.H + kvh * G + g) * p.M + row) * kPartStride;
-        cp_async16(reinterpret_cast<uint8_t*>(pieces) + pi * kPiece + pc * 16,
-                   reinterpret_cast<const uint8_t*>(src) + pc * 16, 16u);
-      }
-      asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-      __syncthreads();
-      for (int k = 0; k < nc; ++k) {
-        const float* o = pieces + (k * G + warp) * kPartStride;
-        const float4 v = *reinterpret_cast<const float4*>(o + d0);
-        const float ca[4] = {v.x, v.y, v.z, v.w};
-        merge_into(r, o[D], o[D + 1], ca);
-      }
-    }
-    merge_into(r, nd[it].m, nd[it].l, nd[it].acc);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float v = __fdiv_rn(r.acc[e], r.l);
-      if (sizeof(T) == 2) reinterpret_cast<uint16_t*>(out)[e] = f32_to_bf16_bits(v);
-      else reinterpret_cast<float*>(out)[e] = v;
-    }
-  }
 }
 
 // ----------------------------------------------------------------- node phase, bf16 (tensor cores)
@@ -938,20 +700,294 @@ __global__ void __launch_bounds__(32) attn_nodes_mma(const AttnDev p, const floa
                    static_cast<uint32_t>(b[2]) | (static_cast<uint32_t>(b[3]) << 16));
   }
 }
-template <typename T, int R>
-static int launch_nodes_r(const AttnDev& p, const float* part, int grid, cudaStream_t stream, bool pdl) {
+// ----------------------------------------------------------------- node phase, fp32 (tensor cores)
+// The node phase of attn_nodes_mma for fp32 data: the same items (one warp per
+// query row x kv head), the same ordered key list cut into batches of 32 by list
+// position, the same online softmax and merge, with every q·k and p·v term the
+// sum of three tf32 products (hi·hi + hi·lo + lo·hi) as in attn_prefix_tf32.
+// S of a batch is four m16n8k8 n-tiles (8 keys each); P·V takes each n-tile as
+// one k-step in the key order (0, 2, 4, 6 | 1, 3, 5, 7), so S's accumulator
+// fragment is the A fragment. The head dims use the permutations of
+// attn_prefix_tf32 (q·k: k-step pair i reads dims 16i + 4t .. +3; P·V n-tile j,
+// position n <- dim 32(j / 4) + 4n + j % 4).
+namespace nf {
+constexpr int kQP = 144, kKP = 144, kVP = 132;   // row pitches (floats): conflict-free fragment reads
+constexpr int kQRows = 16, kListRows = 32;
+constexpr int kQBytes = 2 * kQRows * kQP * 4;    // tf32 hi and lo of q
+constexpr int kKBytes = kListRows * kKP * 4, kVBytes = kListRows * kVP * 4;
+constexpr int kStageBytes = kQBytes + kKBytes + kVBytes;
+// staging | node partials [G][kPartStride] | list slots | mbarrier of the merge's bulk copies
+__host__ __device__ inline int smem_bytes(int G) { return kStageBytes + G * kPartStride * 4 + kListRows * 4 + 16; }
+}  // namespace nf
+
+__global__ void __launch_bounds__(32) attn_nodes_tf32(const AttnDev p, const float* __restrict__ part) {
+  using namespace nf;
+  extern __shared__ __align__(16) uint8_t nsm[];
+  uint32_t* Qh = reinterpret_cast<uint32_t*>(nsm);
+  uint32_t* Ql = Qh + kQRows * kQP;
+  float* Ks = reinterpret_cast<float*>(nsm + kQBytes);
+  float* Vs = reinterpret_cast<float*>(nsm + kQBytes + kKBytes);
   const int G = p.H / p.HK;
-  const int dyn = NodeSmem<T>::bytes(G);
-  if (cudaFuncSetAttribute(attn_nodes<T, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) != cudaSuccess)
-    return RB_ERR_CUDA;
-  return launch_k(attn_nodes<T, R>, dim3(grid), dim3(32 * G), dyn, stream, pdl, p, part);
+  float* npart = reinterpret_cast<float*>(nsm + kStageBytes);                   // [G][kPartStride]
+  int* slots = reinterpret_cast<int*>(nsm + kStageBytes + G * kPartStride * 4);  // [kListRows]
+  const int lane = threadIdx.x, g = lane >> 2, t = lane & 3;
+  const int live = p.sp ? p.sp->q : p.M;
+  const int row = blockIdx.x % p.M, kvh = blockIdx.x / p.M;
+  const uint32_t sbar = smem_u32(nsm + kStageBytes + G * kPartStride * 4 + kListRows * 4);
+  pdl_trigger();
+  if (lane == 0) {
+    mbar_init(sbar, 1);
+    fence_mbar_init();
+  }
+  for (int h = lane; h < G; h += 32) npart[h * kPartStride + 128] = -INFINITY;   // empty node partial
+
+  if (row < live) {
+    // ---- the node fold (needs only q and the node K / V: runs before the wait)
+    const int NP = p.sp ? p.sp->prompt_len : p.NP;
+    const float* kn = p.kn ? static_cast<const float*>(p.kn)
+                           : static_cast<const float*>(p.kp) + static_cast<int64_t>(NP) * p.skpn;
+    const float* vn = p.vn ? static_cast<const float*>(p.vn)
+                           : static_cast<const float*>(p.vp) + static_cast<int64_t>(NP) * p.svpn;
+    const int64_t kbase = static_cast<int64_t>(kvh) * p.sknh, vbase = static_cast<int64_t>(kvh) * p.svnh;
+    const bool trie = p.mask_kind == kMaskTrie;
+    int base = 0, depth = -1;
+    const int32_t* chain = nullptr;
+    if (trie) {
+      base = p.sp ? p.sp->base : p.causal_first;
+      depth = p.depths[row];
+      if (depth < 0 || depth > row || depth >= p.chain_ld) depth = -1;  // invalid trie: reported when the chain was built
+      chain = p.chain + static_cast<int64_t>(row) * p.chain_ld;
+    }
+    // q rows of the group's heads as tf32 hi / lo (rows past G are zero)
+    const float* q = static_cast<const float*>(p.q);
+    for (int i = lane; i < kQRows * 128; i += 32) {
+      const int r = i >> 7, d = i & 127;
+      const float x = r < G ? q[(kvh * G + r) * p.sqh + static_cast<int64_t>(row) * p.sqm + d] : 0.f;
+      uint32_t hi, lo;
+      split_tf32(x, hi, lo);
+      Qh[r * kQP + d] = hi;
+      Ql[r * kQP + d] = lo;
+    }
+    float o[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[j][e] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;   // query heads g and g + 8
+    const float scale2 = p.sm_scale * kLog2e;
+    const int total = trie ? base + depth + 1 : p.NN;
+    // Batches are cut at fixed positions of the row's key list, as in attn_nodes_mma.
+    int scan = 0;   // next candidate to examine
+    while (scan < total) {
+      // 1. the next (up to) 32 list entries
+      int cnt = 0;
+      __syncwarp();   // the previous batch's reads of slots / K / V are done (and q is staged)
+      while (cnt < kListRows && scan < total) {
+        const int i = scan + lane;
+        int slot = 0;
+        bool v;
+        if (trie) {
+          const int ci = i - base;
+          const int cv = (ci >= 0 && ci < p.chain_ld) ? chain[ci] : 0;
+          v = i < total;
+          slot = i < base ? i : base + cv;
+        } else {
+          v = i < total && node_allowed(p, row, i);
+          slot = i;
+        }
+        const unsigned bits = __ballot_sync(0xffffffffu, v);
+        const int rank = __popc(bits & ((1u << lane) - 1u)), room = kListRows - cnt;
+        if (v && rank < room) slots[cnt + rank] = slot;
+        const int n = __popc(bits);
+        if (n <= room) {
+          cnt += n;
+          scan += 32;
+        } else {   // the window holds more than fits: resume at its first entry left out
+          const unsigned left = __ballot_sync(0xffffffffu, v && rank == room);
+          scan += __ffs(left) - 1;
+          cnt = kListRows;
+        }
+      }
+      __syncwarp();
+      if (cnt == 0) break;
+      // 2. stage the entries' K and V rows (rows past cnt zero-filled); lane = 16 bytes of a row
+      for (int u = 0; u < kListRows; ++u) {
+        const bool ok = u < cnt;
+        const int64_t sl = ok ? slots[u] : 0;
+        cp_async16(Ks + u * kKP + 4 * lane, kn + kbase + sl * p.sknn + 4 * lane, ok ? 16u : 0u);
+        cp_async16(Vs + u * kVP + 4 * lane, vn + vbase + sl * p.svnn + 4 * lane, ok ? 16u : 0u);
+      }
+      asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+      __syncwarp();
+      // 3. S = Q K^T over the 32 entries (four 8-entry n-tiles)
+      float sc[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[j][e] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint4 a_g = *reinterpret_cast<const uint4*>(Qh + g * kQP + 16 * i + 4 * t);
+        const uint4 a_g8 = *reinterpret_cast<const uint4*>(Qh + (g + 8) * kQP + 16 * i + 4 * t);
+        const uint4 b_g = *reinterpret_cast<const uint4*>(Ql + g * kQP + 16 * i + 4 * t);
+        const uint4 b_g8 = *reinterpret_cast<const uint4*>(Ql + (g + 8) * kQP + 16 * i + 4 * t);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float4 kv = *reinterpret_cast<const float4*>(Ks + (j * 8 + g) * kKP + 16 * i + 4 * t);
+          uint32_t kh[4], kl[4];
+          split_tf32_fast(kv.x, kh[0], kl[0]);
+          split_tf32_fast(kv.y, kh[1], kl[1]);
+          split_tf32_fast(kv.z, kh[2], kl[2]);
+          split_tf32_fast(kv.w, kh[3], kl[3]);
+          // k-step 2i: dims 16i + 4t + {0, 1}; k-step 2i + 1: dims 16i + 4t + {2, 3}
+          mma_tf32_1688(sc[j], a_g.x, a_g8.x, a_g.y, a_g8.y, kh[0], kh[1]);
+          mma_tf32_1688(sc[j], a_g.z, a_g8.z, a_g.w, a_g8.w, kh[2], kh[3]);
+          mma_tf32_1688(sc[j], a_g.x, a_g8.x, a_g.y, a_g8.y, kl[0], kl[1]);
+          mma_tf32_1688(sc[j], a_g.z, a_g8.z, a_g.w, a_g8.w, kl[2], kl[3]);
+          mma_tf32_1688(sc[j], b_g.x, b_g8.x, b_g.y, b_g8.y, kh[0], kh[1]);
+          mma_tf32_1688(sc[j], b_g.z, b_g8.z, b_g.w, b_g8.w, kh[2], kh[3]);
+        }
+      }
+      // 4. online softmax of rows g and g + 8 (entries past cnt masked)
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          if (j * 8 + 2 * t + e >= cnt) sc[j][e] = sc[j][2 + e] = -INFINITY;
+          mx0 = fmaxf(mx0, sc[j][e]);
+          mx1 = fmaxf(mx1, sc[j][2 + e]);
+        }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float n0 = fmaxf(m0, mx0 * scale2), n1 = fmaxf(m1, mx1 * scale2);
+      const float al0 = fast_exp2(m0 - n0), al1 = fast_exp2(m1 - n1);
+      float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          sc[j][e] = fast_exp2(fmaf(sc[j][e], scale2, -n0));
+          sc[j][2 + e] = fast_exp2(fmaf(sc[j][2 + e], scale2, -n1));
+          rs0 += sc[j][e];
+          rs1 += sc[j][2 + e];
+        }
+      rs0 += __shfl_xor_sync(0xffffffffu, rs0, 1);
+      rs0 += __shfl_xor_sync(0xffffffffu, rs0, 2);
+      rs1 += __shfl_xor_sync(0xffffffffu, rs1, 1);
+      rs1 += __shfl_xor_sync(0xffffffffu, rs1, 2);
+      l0 = fmaf(l0, al0, rs0);
+      l1 = fmaf(l1, al1, rs1);
+      m0 = n0;
+      m1 = n1;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        o[j][0] *= al0; o[j][1] *= al0;
+        o[j][2] *= al1; o[j][3] *= al1;
+      }
+      // 5. O += P V: n-tile kc of S is the k-step over keys 8kc + (2t, 2t + 1)
+#pragma unroll
+      for (int kc = 0; kc < 4; ++kc) {
+        uint32_t ph[4], pl[4];
+        split_tf32_fast(sc[kc][0], ph[0], pl[0]);   // (g, key 2t)
+        split_tf32_fast(sc[kc][2], ph[1], pl[1]);   // (g + 8, key 2t)
+        split_tf32_fast(sc[kc][1], ph[2], pl[2]);   // (g, key 2t + 1)
+        split_tf32_fast(sc[kc][3], ph[3], pl[3]);   // (g + 8, key 2t + 1)
+        const float* v0r = Vs + (kc * 8 + 2 * t) * kVP + 4 * g;
+        const float* v1r = v0r + kVP;
+#pragma unroll
+        for (int jq = 0; jq < 4; ++jq) {
+          const float4 va = *reinterpret_cast<const float4*>(v0r + 32 * jq);
+          const float4 vb = *reinterpret_cast<const float4*>(v1r + 32 * jq);
+          const float a4[4] = {va.x, va.y, va.z, va.w}, b4[4] = {vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+          for (int jr = 0; jr < 4; ++jr) {
+            uint32_t h0, l0b, h1, l1b;
+            split_tf32_fast(a4[jr], h0, l0b);
+            split_tf32_fast(b4[jr], h1, l1b);
+            mma_3xtf32(o[jq * 4 + jr], ph, pl, h0, h1, l0b, l1b);
+          }
+        }
+      }
+    }
+    // the node partial of every head of the group: acc[128], m, l
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int h = g + half * 8;
+      if (h < G) {
+        float* np = npart + h * kPartStride;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int d = 32 * (j >> 2) + 8 * t + (j & 3);
+          np[d] = o[j][2 * half];
+          np[d + 4] = o[j][2 * half + 1];
+        }
+        if (t == 0) {
+          np[128] = half ? m1 : m0;
+          np[129] = half ? l1 : l0;
+        }
+      }
+    }
+  }
+
+  pdl_wait();  // the prefix chunk partials are complete
+  const int NP = p.sp ? p.sp->prompt_len : p.NP;
+  const int nchunks = prefix_nchunks(NP, p.H);
+  const int d0 = lane * 4;
+  float* out = static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.som + d0;
+  if (row >= live) {  // padding row: zeros, no reads
+    for (int h = 0; h < G; ++h)
+      *reinterpret_cast<float4*>(out + (kvh * G + h) * p.soh) = make_float4(0.f, 0.f, 0.f, 0.f);
+    return;
+  }
+  // The row's chunk partials, one bulk copy per 528-byte piece on one mbarrier:
+  // all of them when they fit, else one head's chunks at a time.
+  constexpr int kPiece = kPartStride * 4;
+  float* pieces = reinterpret_cast<float*>(nsm);
+  const int cap_pieces = kStageBytes / kPiece;
+  const bool all_at_once = G * nchunks <= cap_pieces;
+  uint32_t sphase = 0;
+  auto stage = [&](int h_first, int h_count) {   // pieces (chunk k, head h_first + j) at index j * nchunks + k
+    fence_proxy_async_smem();   // this lane's generic accesses of the staging area come before the copies' writes
+    __syncwarp();
+    const int n = h_count * nchunks;
+    if (lane == 0) mbar_arrive_expect_tx(sbar, static_cast<uint32_t>(n * kPiece));
+    __syncwarp();
+    for (int pi = lane; pi < n; pi += 32) {
+      const int k = pi % nchunks, hh = h_first + pi / nchunks;
+      const float* src = part + ((static_cast<int64_t>(k) * p.H + kvh * G + hh) * p.M + row) * kPartStride;
+      bulk_load(smem_u32(reinterpret_cast<uint8_t*>(pieces) + pi * kPiece), src, kPiece, sbar);
+    }
+    const bool ok = mbar_wait(sbar, sphase, 0x232);
+    sphase ^= 1u;
+    __syncwarp();
+    return ok;
+  };
+  __syncwarp();   // the node partial written by the fold is visible to every lane
+  if (all_at_once && nchunks > 0 && !stage(0, G)) return;
+  for (int h = 0; h < G; ++h) {
+    if (!all_at_once && nchunks > 0 && !stage(h, 1)) return;
+    const float* ph = pieces + (all_at_once ? h * nchunks : 0) * kPartStride;
+    // prefix chunk partials in ascending chunk order, then the node partial
+    NodeAcc r{-INFINITY, 0.f, {0.f, 0.f, 0.f, 0.f}};
+    for (int k = 0; k < nchunks; ++k) {
+      const float* o = ph + k * kPartStride;
+      const float4 v = *reinterpret_cast<const float4*>(o + d0);
+      const float ca[4] = {v.x, v.y, v.z, v.w};
+      merge_into(r, o[128], o[129], ca);
+    }
+    const float* np = npart + h * kPartStride;
+    const float4 v = *reinterpret_cast<const float4*>(np + d0);
+    const float ca[4] = {v.x, v.y, v.z, v.w};
+    merge_into(r, np[128], np[129], ca);
+    *reinterpret_cast<float4*>(out + (kvh * G + h) * p.soh) =
+        make_float4(__fdiv_rn(r.acc[0], r.l), __fdiv_rn(r.acc[1], r.l), __fdiv_rn(r.acc[2], r.l),
+                    __fdiv_rn(r.acc[3], r.l));
+  }
 }
 
-// Items per block. One: a block's items run one after another (each a chain
-// of dependent loads, a block barrier per batch and a serial fold), so under
-// PDL more items per block made the pre-wait part outlast the prefix kernel
-// (measured on the config-3 step: 9.7 us after the prefix with one item,
-// 17.8 with two, 17.3 with three), so only R = 1 is built.
 template <typename T>
 static int launch_nodes(const AttnDev& p, const float* part, cudaStream_t stream, bool pdl) {
   const int G = p.H / p.HK;
@@ -964,7 +1000,12 @@ static int launch_nodes(const AttnDev& p, const float* part, cudaStream_t stream
       return RB_ERR_CUDA;
     return launch_k(attn_nodes_mma, dim3(items), dim3(32), dyn, stream, pdl, p, part);
   }
-  return launch_nodes_r<T, 1>(p, part, items, stream, pdl);
+  static_assert(sizeof(T) == 2 || sizeof(T) == 4, "bf16 or fp32 data");
+  // fp32: one warp per item, three tf32 products per term
+  const int dyn = nf::smem_bytes(G);
+  if (cudaFuncSetAttribute(attn_nodes_tf32, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) != cudaSuccess)
+    return RB_ERR_CUDA;
+  return launch_k(attn_nodes_tf32, dim3(items), dim3(32), dyn, stream, pdl, p, part);
 }
 
 // ----------------------------------------------------------------- host
