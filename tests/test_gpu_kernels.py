@@ -163,31 +163,32 @@ def test_attention_layout_sweep(dtype):
         assert torch.equal(outs[0], o)
 
 
-def test_attention_row_count_and_mask_kind_invariance():
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_attention_row_count_and_mask_kind_invariance(dtype):
     from respect_b200.kernels.attention import attn_call
     from respect_b200 import _lib
     rng = np.random.default_rng(1)
     seqs = top_up(rng, chain_seqs(rng, 4, 32, 50), 128, 50)
     c = attention_case(3, NP=3000, seqs=seqs, committed=9)
-    b = {k: T(round_bf16(c[k]), torch.bfloat16) for k in ("q", "kp", "vp", "kn", "vn")}
+    b = {k: T(round_bf16(c[k]), dtype) for k in ("q", "kp", "vp", "kn", "vn")}
     msk = T(c["msk"], torch.bool)
     full = torch.empty_like(b["q"])
     attn_call(b["q"], b["kp"], b["vp"], b["kn"], b["vn"], msk, full, 128 ** -0.5)
-    # additive bf16 mask (dispatch passes allow = mask == 0)
-    add = torch.where(msk, 0.0, torch.finfo(torch.bfloat16).min).to(torch.bfloat16)
+    # additive mask in the data's dtype (dispatch passes allow = mask == 0)
+    add = torch.where(msk, 0.0, torch.finfo(dtype).min).to(dtype)
     o2 = torch.empty_like(full)
     attn_call(b["q"], b["kp"], b["vp"], b["kn"], b["vn"], add, o2, 128 ** -0.5)
     assert torch.equal(full, o2)
     # every row alone (M = 1) equals its row of the full call
     for r in (0, 1, 63, 64, 100, 127):
-        o1 = torch.empty(28, 1, 128, device=DEV, dtype=torch.bfloat16)
+        o1 = torch.empty(28, 1, 128, device=DEV, dtype=dtype)
         attn_call(b["q"][:, r:r + 1], b["kp"], b["vp"], b["kn"], b["vn"], msk[r:r + 1], o1, 128 ** -0.5)
         assert torch.equal(o1[:, 0], full[:, r])
     # causal mode equals the explicit causal bool mask
     NN = b["kn"].shape[1]
     first = NN - 16 - 3
     cm = (torch.arange(NN, device=DEV)[None, :] <= torch.arange(16, device=DEV)[:, None] + first)
-    o3 = torch.empty(28, 16, 128, device=DEV, dtype=torch.bfloat16)
+    o3 = torch.empty(28, 16, 128, device=DEV, dtype=dtype)
     o4 = torch.empty_like(o3)
     attn_call(b["q"][:, :16], b["kp"], b["vp"], b["kn"], b["vn"], cm, o3, 128 ** -0.5)
     attn_call(b["q"][:, :16], b["kp"], b["vp"], b["kn"], b["vn"], None, o4, 128 ** -0.5,
