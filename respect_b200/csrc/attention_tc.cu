@@ -6,7 +6,7 @@
 //   S = Q K^T            tcgen05.mma, M=128 rows, N=128 keys, K=128 dims -> TMEM
 //   m' = max(m, rowmax(S*scale)); alpha = 2^(m - m'); p = 2^(S*scale - m')
 //   O = O*alpha (in TMEM, by the softmax threads); l = l*alpha + sum(p)
-//   O += bf16(p) V       tcgen05.mma, A = P (smem, K-major), B = V (MN-major)
+//   O += bf16(p) V       tcgen05.mma, A = P (TMEM, written by the softmax threads), B = V (MN-major)
 // The output accumulator never leaves TMEM until the chunk is done, so the
 // softmax of tile j+1 runs while the tensor core computes P_j V_j.
 //
@@ -29,8 +29,9 @@ constexpr int kHalf = 128 * 64 * 2;          // one 64-element-wide swizzled hal
 constexpr int kQOff = 0;                     // Q: 2 halves
 constexpr int kKVOff = 2 * kHalf;            // 2 stages x (K 2 halves, V 2 halves)
 constexpr int kStage = 4 * kHalf;            // 64 KB
-constexpr int kPOff = kKVOff + 2 * kStage;   // P: 2 halves (keys 0-63 | 64-127)
-constexpr int kBarOff = kPOff + 2 * kHalf;   // 192 KB
+constexpr int kBarOff = kKVOff + 2 * kStage;   // 160 KB
+// TMEM columns: S double buffer 0-255, O 256-383, P (bf16 pairs, 64 columns) from 384
+constexpr uint32_t kPCol = 384;
 constexpr int kRedOff = kBarOff + 256;       // row max / row sum exchange: [2 tiles][2][2 halves][128] floats
 constexpr int kSmem = 1024 + kRedOff + 1024 * 4;
 static_assert(kSmem <= 232448, "shared memory budget");
@@ -104,7 +105,7 @@ __global__ void __maxnreg__(136)
   const uint32_t tmem = *tmem_slot;
   pdl_wait();  // q / K / V come from the previous kernels
   pdl_trigger();
-  const uint32_t sQ = smem_u32(smem + kQOff), sKV = smem_u32(smem + kKVOff), sP = smem_u32(smem + kPOff);
+  const uint32_t sQ = smem_u32(smem + kQOff), sKV = smem_u32(smem + kKVOff);
 
   if (warp == kProducerWarp) {
     if (lane == 0) {  // TMA producer
@@ -159,9 +160,9 @@ __global__ void __maxnreg__(136)
         const uint32_t sv = sKV + (j & 1) * kStage + 2 * kHalf;
 #pragma unroll
         for (int kk = 0; kk < kKeys / 16; ++kk) {
-          const uint32_t pa = sP + (kk >> 2) * kHalf + (kk & 3) * 32;
-          umma_bf16(tmem + 256, sdesc_kmajor_sw128(pa), sdesc_mnmajor_sw128(sv + kk * 2048, kHalf), kIdescPV,
-                    (j | kk) ? 1u : 0u);
+          // A = P from tensor memory: keys 16kk .. 16kk + 15 are columns kPCol + 8kk ..
+          umma_bf16_ta(tmem + 256, tmem + kPCol + kk * 8, sdesc_mnmajor_sw128(sv + kk * 2048, kHalf), kIdescPV,
+                       (j | kk) ? 1u : 0u);
         }
         umma_commit(bar(O_FULL));
         if (j + 2 < ntiles) umma_commit(bar(V_EMPTY + (j & 1)));  // V(j) read: the stage takes V(j+2)
@@ -266,15 +267,16 @@ __global__ void __maxnreg__(136)
           tmem_wait_st();
         }
       }
-      if (ok) {
-        uint8_t* rowp = smem + kPOff + hf * kHalf + r * 128;
+      if (ok) {  // P of this thread's row and 64 keys: columns kPCol + 32 hf .. + 31 of its lane
+        const uint32_t pb = lane_base + kPCol + hf * 32;
+        uint32_t w0[16], w1[16];
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc)  // 8 keys = one 16-byte chunk of the swizzled row
-          *reinterpret_cast<uint4*>(rowp + ((cc ^ (r & 7)) << 4)) =
-              make_uint4(w[cc * 4], w[cc * 4 + 1], w[cc * 4 + 2], w[cc * 4 + 3]);
+        for (int i = 0; i < 16; ++i) { w0[i] = w[i]; w1[i] = w[16 + i]; }
+        tmem_st16(pb, w0);
+        tmem_st16(pb + 16, w1);
+        tmem_wait_st();
       }
-      fence_proxy_async_smem();  // P stores -> visible to the tensor core (async proxy)
-      tc_fence_before();         // S loads and O stores of this tile ordered before the arrive
+      tc_fence_before();         // S loads, O and P stores of this tile ordered before the arrive
       mbar_arrive(bar(P_FULL));
       alpha_prev = alpha;
       m = m_new;
